@@ -1,0 +1,398 @@
+"""Compile driver for the `cuda` target: a PyTorch module or an anvil.graph module -> CompiledModel whose run()
+executes on B200s through libanvil_cuda.so.
+
+Mirrors the reference driver anvil/driver.py (RunOutput :56-76, _resolve_model :90-116, _checked_graph :119-132,
+CompiledModel :168-327, compile :330-335) with the tiny-gpu lowering/scheduling/codegen replaced by
+anvil.runtime.program (graph -> launch list) and the simulator dispatch replaced by the `cuda` backend:
+
+    cm = anvil.compile(block, (x_example,), calib)          # torch module: capture + quantize (anvil.frontend)
+    cm = anvil.compile(module, consts=consts)               # graph IR (+ consts), proved free of int32 overflow
+    res = cm.run(x_float, "cuda")                           # quantize x, run on the GPU, read back, dequantize
+    res = cm.run(xq, "cuda", quantized=True)                # integer inputs
+    res.output, res.ints["out"], res.cycles                 # float output, int values, per-kernel device us
+    print(cm.summary())
+
+Batching: where the reference runs one sample per job, the cuda target also takes a leading batch dim on every
+input (all inputs the same batch); values then carry it, exactly as the oracle's batch=True evaluation. With
+CudaParams(devices=(0, 1, ...)) the batch is split into contiguous shards, one per device, each device running
+its own replica of the const region and launch list; there is no collective on the compute path.
+"""
+from __future__ import annotations
+
+import math
+import threading
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .ir import graph as g
+
+BACKENDS = ("cuda",)
+
+
+@dataclass(frozen=True)
+class CudaParams:
+    """Execution parameters of the cuda target (the analogue of the reference's GpuParams, api.py:22-63).
+
+    devices   CUDA device ordinals; a batch is sharded across them (contiguous, ceil(B / G) each)
+    checked   check every int32 intermediate on the device (OverflowError like the oracle); None: only when
+              the static overflow proof does not hold for the graph
+    fuse      apply launch fusions (LUT epilogues, fused attention); keep="all" runs disable them
+    gemm      "auto" | "tc" (tcgen05 wherever the shape allows) | "simt" (CUDA-core kernel everywhere)
+    """
+    devices: tuple = (0,)
+    checked: bool | None = None
+    fuse: bool = True
+    gemm: str = "auto"
+
+    def __post_init__(self):
+        if not self.devices or any(not isinstance(d, int) or d < 0 for d in self.devices):
+            raise ValueError(f"CudaParams.devices = {self.devices!r}: need non-negative ints")
+        if self.gemm not in ("auto", "tc", "simt"):
+            raise ValueError(f"CudaParams.gemm = {self.gemm!r}: auto, tc or simt")
+
+
+@dataclass
+class RunOutput:
+    output: np.ndarray                  # first graph output, dequantized (float)
+    outputs: list                       # every graph output, dequantized
+    ints: dict                          # sym -> int array of every value readable after the run
+    cycles: dict                        # launch label -> device microseconds (None unless run(..., timing=True))
+    result: object = None               # CudaRunResult
+    job: object = None                  # the DeviceProgram of device 0
+
+    @property
+    def total_cycles(self):
+        c = list(self.cycles.values())
+        return None if any(v is None for v in c) else sum(c)
+
+
+@dataclass
+class CudaRunResult:
+    batch: int
+    shards: list                        # [(device, batch)]
+    kernel_us: dict = field(default_factory=dict)
+
+
+def _resolve_model(model, example_inputs, calib_inputs, consts, quant_kw, prove=True):
+    from .frontend import Quantized
+    from .frontend.numerics import prove_no_overflow
+
+    graph_path = isinstance(model, (Quantized, g.Module)) or (
+        isinstance(model, tuple) and len(model) == 2 and isinstance(model[0], g.Module))
+    if graph_path and quant_kw:
+        raise TypeError(f"anvil.compile got unexpected keyword argument(s) {sorted(quant_kw)} (extra keywords go to "
+                        "quantize, which only runs for a torch module)")
+    if isinstance(model, Quantized):
+        return model.module, dict(model.consts), model
+    if isinstance(model, tuple) and len(model) == 2 and isinstance(model[0], g.Module):
+        return _checked_graph(model[0], dict(model[1]), prove, prove_no_overflow)
+    if isinstance(model, g.Module):
+        return _checked_graph(model, dict(consts or {}), prove, prove_no_overflow)
+    try:
+        import torch
+    except ImportError:
+        torch = None
+    if torch is not None and isinstance(model, torch.nn.Module):
+        from .frontend import from_torch
+        if example_inputs is None or calib_inputs is None:
+            raise ValueError("compiling a torch module needs example_inputs and calib_inputs")
+        q = from_torch(model, example_inputs, calib_inputs, **quant_kw)
+        return q.module, dict(q.consts), q
+    raise TypeError(f"cannot compile a {type(model).__name__}: expected a torch.nn.Module, anvil.frontend.Quantized, "
+                    "an anvil.graph module or (module, consts)")
+
+
+def _checked_graph(module, consts, prove, prove_fn):
+    """Every non-inline const needs its values and, unless prove=False, the int32 overflow proof must hold
+    (anvil/driver.py:119-132). prove=False compiles anyway and runs every kernel in checked mode."""
+    need = [op.sym_str for op in g.func_of(module).ops if isinstance(op, g.ConstOp) and op.value is None]
+    missing = [s for s in need if s not in consts]
+    if missing:
+        raise ValueError(f"no values for graph consts {missing}: pass consts= or a (module, consts) pair")
+    unknown = sorted(set(consts) - set(need))
+    if unknown:
+        raise ValueError(f"consts {unknown} name no graph const of the module")
+    if prove:
+        prove_fn(module, consts)
+    return module, consts, None
+
+
+class CompiledModel:
+    """A graph ready for the cuda target: per batch size a lowered launch list and memory plan, per device a
+    replica of the const region (built lazily on the first run)."""
+
+    def __init__(self, module, consts, params: CudaParams | None = None, *, quantized=None, proven=None):
+        from .frontend.numerics import prove_no_overflow
+
+        if isinstance(params, dict):
+            params = CudaParams(**params)
+        self.params = params or CudaParams()
+        if not isinstance(self.params, CudaParams):
+            raise TypeError(f"params must be a CudaParams (or a dict of its fields), not {type(self.params).__name__}")
+        self.module, self.consts, self.quantized = module, consts, quantized
+        self.func = g.func_of(module)
+        if not [op for op in self.func.ops if not isinstance(op, (g.InputOp, g.ConstOp, g.OutputOp))]:
+            raise ValueError("the graph has no operations to compile (its outputs are its inputs)")
+        self.meta = g.graph_meta(module)
+        self.in_dtypes = {op.sym_str: g.qt(op.result).dtype for op in self.func.ops if isinstance(op, g.InputOp)}
+        if proven is None:
+            try:
+                prove_no_overflow(module, consts)
+                proven = True
+            except (OverflowError, ValueError):
+                proven = False
+        self.proven = proven
+        self.checked = (not proven) if self.params.checked is None else bool(self.params.checked)
+        from .runtime.program import ConstPool
+        self._pool = ConstPool()
+        self._programs = {}          # (batch, keep) -> DeviceProgram
+        self._devices = {}           # device -> DeviceModel
+        self._pool_size_at_upload = {}
+        self._lock = threading.Lock()
+
+    # ------------------------------------------------------------------------------------- programs
+    def program(self, batch: int = 1, keep: str = "outputs"):
+        from .runtime.program import lower_program
+        key = (int(batch), keep)
+        if key not in self._programs:
+            self._programs[key] = lower_program(self.module, self.consts, self._pool, batch, keep,
+                                                checked=self.checked, fuse=self.params.fuse, gemm=self.params.gemm)
+        return self._programs[key]
+
+    @property
+    def plan(self):
+        return self.program(1).plan
+
+    @property
+    def footprint(self) -> int:
+        return self.plan.footprint
+
+    def _device_model(self, device: int):
+        from .runtime.cuda import DeviceModel
+        dm = self._devices.get(device)
+        if dm is None or self._pool_size_at_upload.get(device) != self._pool.size:
+            if dm is not None:
+                dm.close()
+            dm = DeviceModel(device, self._pool.blob())
+            self._devices[device] = dm
+            self._pool_size_at_upload[device] = self._pool.size
+        return dm
+
+    # -------------------------------------------------------------------------------- (de)quantization
+    @property
+    def inputs(self) -> list:
+        return [op.sym_str for op in self.func.ops if isinstance(op, g.InputOp)]
+
+    @property
+    def outputs(self) -> list:
+        for op in self.func.ops:
+            if isinstance(op, g.OutputOp):
+                return [v.owner.sym_str for v in op.values]
+        return []
+
+    def scale(self, sym):
+        return self.meta[sym][0]
+
+    def quantize_input(self, x, sym=None):
+        """Float array -> integers by the input's scale (round half to even, saturating at the input's dtype;
+        anvil/driver.py:233-241)."""
+        sym = sym or self.inputs[0]
+        s = self.scale(sym)
+        if s is None:
+            raise ValueError(f"input {sym!r} has no scale: pass integer inputs with quantized=True")
+        lo, hi = {"i8": (-128, 127), "i16": (-(1 << 15), (1 << 15) - 1), "i32": (-(1 << 31), (1 << 31) - 1)}[
+            self.meta[sym][2]]
+        return np.clip(np.rint(np.asarray(x, dtype=np.float64) / s), lo, hi).astype(np.int64)
+
+    def dequantize(self, sym, ints):
+        s = self.scale(sym)
+        return np.asarray(ints, dtype=np.float64) * (1.0 if s is None else s)
+
+    def _bind_inputs(self, x, quantized):
+        """-> ({sym: array with a leading batch dim}, batch, batched?)."""
+        xs = list(x) if isinstance(x, (list, tuple)) else [x]
+        if len(xs) != len(self.inputs):
+            raise ValueError(f"{len(xs)} inputs for graph inputs {self.inputs}")
+        out, batch, batched = {}, None, None
+        for sym, v in zip(self.inputs, xs):
+            v = np.asarray(v)
+            shape = tuple(self.meta[sym][1])
+            if v.shape == shape:
+                b, v = 1, v.reshape((1,) + shape)
+                isb = False
+            elif v.ndim == len(shape) + 1 and tuple(v.shape[1:]) == shape:
+                b, isb = v.shape[0], True
+            elif v.size == math.prod(shape) and (v.ndim <= 1 or tuple(d for d in v.shape if d != 1) == tuple(
+                    d for d in shape if d != 1)):
+                # a flat array or extra size-1 dims (anvil/driver.py:254-261); a transposed input is an error
+                b, v, isb = 1, v.reshape((1,) + shape), False
+            else:
+                raise ValueError(f"input {sym!r}: shape {v.shape} != {shape} (or a leading batch dim + {shape})")
+            if b < 1:
+                raise ValueError(f"input {sym!r}: empty batch")
+            if batch is not None and (b != batch or isb != batched):
+                raise ValueError(f"inputs disagree on the batch: {batch} vs {b}")
+            batch, batched = b, isb
+            out[sym] = self._check_int_input(sym, v) if quantized else self._quantize_checked(sym, v)
+        return out, batch, batched
+
+    def _quantize_checked(self, sym, v):
+        if self.meta[sym][0] is None:
+            raise ValueError(f"input {sym!r} has no scale: pass integer inputs with quantized=True")
+        if not np.all(np.isfinite(np.asarray(v, dtype=np.float64))):
+            raise ValueError(f"input {sym!r} has NaN or infinite values")
+        return self.quantize_input(v, sym)
+
+    def _check_int_input(self, sym, v):
+        """quantized=True: integer values inside the input's own dtype (anvil/driver.py:270-280)."""
+        if v.dtype.kind not in "iub":
+            raise ValueError(f"input {sym!r}: quantized=True needs integer values, got dtype {v.dtype}")
+        dt = self.in_dtypes.get(sym, "i8")
+        bits = {"i8": 8, "i16": 16, "i32": 32}[dt]
+        lo, hi = -(1 << (bits - 1)), (1 << (bits - 1)) - 1
+        if v.size and (int(v.min()) < lo or int(v.max()) > hi):
+            raise ValueError(f"input {sym!r}: values in [{v.min()}, {v.max()}] outside {dt} [{lo}, {hi}]")
+        return v
+
+    # --------------------------------------------------------------------------------------------- runs
+    def run(self, x, backend: str = "cuda", *, quantized=False, keep="outputs", timing=False) -> RunOutput:
+        """Quantize `x` (unless quantized=True), run the launch chain on the GPU(s), read back."""
+        if backend not in BACKENDS:
+            raise ValueError(f"unknown backend {backend!r}: this build runs {', '.join(BACKENDS)} (the tiny-gpu "
+                             "simulators isasim/rtl/verilator are not part of it)")
+        if keep not in ("outputs", "all"):
+            raise ValueError(f"keep must be 'outputs' or 'all', not {keep!r}")
+        bound, batch, batched = self._bind_inputs(x, quantized)
+        ints, kus, shards = self._run_cuda(bound, batch, keep, timing)
+        if not batched:
+            ints = {k: v[0] if v.ndim and v.shape[0] == 1 and k not in self._const_syms() else v
+                    for k, v in ints.items()}
+        outs = [self.dequantize(s, ints[s]) for s in self.outputs]
+        prog = self.program(shards[0][1], keep)
+        cycles = {}
+        for d, us in zip(prog.devops, kus if kus is not None else [None] * len(prog.devops)):
+            cycles[d.label] = (cycles.get(d.label) or 0) + us if us is not None else None
+        return RunOutput(outs[0], outs, ints, cycles, CudaRunResult(batch, shards, cycles), prog)
+
+    def _const_syms(self):
+        return {op.sym_str for op in self.func.ops if isinstance(op, g.ConstOp)}
+
+    def _shards(self, batch):
+        devs = list(self.params.devices)
+        n = min(len(devs), batch)
+        per = -(-batch // n)
+        out, lo = [], 0
+        for d in devs[:n]:
+            hi = min(batch, lo + per)
+            if hi > lo:
+                out.append((d, lo, hi))
+            lo = hi
+        return out
+
+    def _run_cuda(self, bound, batch, keep, timing):
+        shards = self._shards(batch)
+        results, errors = [None] * len(shards), [None] * len(shards)
+
+        def work(i, dev, lo, hi):
+            try:
+                results[i] = self._run_shard(dev, {k: v[lo:hi] for k, v in bound.items()}, hi - lo, keep, timing)
+            except BaseException as e:            # re-raised on the calling thread
+                errors[i] = e
+
+        with self._lock:
+            for b in {hi - lo for _, lo, hi in shards}:        # lower (and pack consts) before any upload
+                self.program(b, keep)
+            if len(shards) == 1:
+                work(0, *shards[0])
+            else:
+                ts = [threading.Thread(target=work, args=(i, *s)) for i, s in enumerate(shards)]
+                for t in ts:
+                    t.start()
+                for t in ts:
+                    t.join()
+        for e in errors:
+            if e is not None:
+                raise e
+        ints = {}
+        for k in results[0][0]:
+            parts = [r[0][k] for r in results]
+            ints[k] = parts[0] if k in self._const_syms() else np.concatenate(parts, axis=0)
+        return ints, results[0][1], [(d, hi - lo) for d, lo, hi in shards]
+
+    def _run_shard(self, device, bound, b, keep, timing):
+        prog = self.program(b, keep)
+        dm = self._device_model(device)
+        if dm.prepared_key != (b, keep):
+            dm.prepare(prog.ops, prog.plan.arena, key=(b, keep))
+        ins = []
+        for sym, (off, shape, dtype) in prog.inputs.items():
+            arr = np.ascontiguousarray(bound[sym], dtype={"i8": np.int8, "i16": np.int16, "i32": np.int32}[dtype])
+            ins.append((off, arr))
+        want = self._readable(prog, keep)
+        roots = {}
+        for sym, v in want.items():
+            roots.setdefault(v.root, None)
+        outs = []
+        for r in roots:
+            buf = np.empty(prog.buffers[r], dtype=np.uint8)
+            roots[r] = buf
+            outs.append((prog.plan.addresses[r], buf))
+        kus = dm.run(ins, outs, timing=timing)
+        ints = {}
+        for sym, v in want.items():
+            ints[sym] = _apply_view(roots[v.root], v)
+        for sym in self.inputs:
+            ints.setdefault(sym, np.asarray(bound[sym], dtype=np.int64))
+        return ints, kus
+
+    def _readable(self, prog, keep):
+        want = {}
+        for sym, v in prog.outputs:
+            if not v.const and sym is not None:
+                want[sym] = v
+        if keep == "all":
+            for sym, v in prog.views.items():
+                want.setdefault(sym, v)
+        return want
+
+    def readable(self, keep="outputs") -> list:
+        prog = self.program(1, keep)
+        return list(self._readable(prog, keep)) + [s for s in self.inputs]
+
+    # ------------------------------------------------------------------------------------------ summary
+    def summary(self, batch: int = 1, kernel_us: dict | None = None) -> str:
+        """Per launch: label, kernel, shape, algorithmic ops / bytes (and measured us when given), then the plan."""
+        from .runtime.cuda import KIND_NAMES
+        prog = self.program(batch)
+        rows = []
+        for i, d in enumerate(prog.devops):
+            f = d.fields
+            kname = KIND_NAMES.get(d.kind, str(d.kind))
+            if d.kind == 1:
+                kname += "[simt]" if f.get("flags", 0) & 32 else "[tcgen05]"
+            dims = "x".join(str(v) for v in f.get("dims", []))
+            w = d.work
+            work = (f"{w['ops'] / 1e6:10.2f} Mop" if "ops" in w else f"{w.get('bytes', 0) / 1e6:10.2f} MB ")
+            t = "" if not kernel_us or d.label not in kernel_us else f" {kernel_us[d.label]:9.2f} us"
+            rows.append(f"{d.label:>16} {kname:<18} {dims:<24} {work}{t}")
+        extra = [f"fusions: {', '.join(prog.fused) or 'none'}", f"checked: {self.checked} (proof "
+                 f"{'holds' if self.proven else 'fails'})", prog.plan.report()]
+        return "\n".join(rows + extra)
+
+
+def _apply_view(buf: np.ndarray, v) -> np.ndarray:
+    from .runtime.program import NP
+    arr = buf.view(NP[v.dtype])
+    isz = arr.itemsize
+    out = np.lib.stride_tricks.as_strided(arr[v.offset:], v.shape, [s * isz for s in v.strides])
+    return np.array(out, dtype=np.int64)
+
+
+def compile(model, example_inputs=None, calib_inputs=None, params: CudaParams | None = None, schedules=None, *,
+            consts=None, prove=True, **quant_kw) -> CompiledModel:  # noqa: A001
+    """anvil.compile (anvil/driver.py:330-335). `schedules` is accepted for signature parity and ignored: the
+    cuda target picks its kernels from the shapes. prove=False skips the static int32 proof for a graph-IR model
+    and runs every kernel in checked mode instead."""
+    module, cs, q = _resolve_model(model, example_inputs, calib_inputs, consts, quant_kw, prove)
+    return CompiledModel(module, cs, params, quantized=q)

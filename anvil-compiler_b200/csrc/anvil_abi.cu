@@ -1,0 +1,647 @@
+// libanvil_cuda.so: the C-ABI declared in include/anvil_cuda.h and the runtime behind it.
+//
+// A model owns, on one device: the const region (weights, LUTs, biases in device layout, uploaded once), an
+// activation arena laid out by the host's liveness plan (anvil/memplan.py:190-198, in bytes), a small flag array
+// the checked kernels write, and one non-blocking stream. anvil_model_prepare turns the host's anvil_op list into
+// resolved launches (device pointers, grid sizes, TMA tensor maps) after checking every byte range each op
+// touches against the region it lives in; anvil_model_run then only copies and launches.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/anvil_cuda.h"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "rowops.cuh"
+
+using namespace anvil;
+
+// --------------------------------------------------------------------------------------------- error state
+
+static thread_local std::string g_err = "";
+
+static int fail(int code, const char *fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+#define CK(call)                                                                                          \
+  do {                                                                                                    \
+    cudaError_t e_ = (call);                                                                              \
+    if (e_ != cudaSuccess) return fail(e_ == cudaErrorMemoryAllocation ? ANVIL_E_OOM : ANVIL_E_CUDA,      \
+                                       "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, \
+                                       __LINE__);                                                         \
+  } while (0)
+
+extern "C" int anvil_abi_version(void) { return ANVIL_ABI_VERSION; }
+extern "C" const char *anvil_last_error(void) { return g_err.c_str(); }
+
+// ------------------------------------------------------------------------------------ driver entry points
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// int8 tensor map over a (z, y, x) array with x contiguous: box = (1, box_y, 128 bytes), 128-byte swizzle.
+static int make_map_i8(CUtensorMap *map, const void *base, uint64_t x, uint64_t y, uint64_t z, uint64_t ystride,
+                       uint64_t zstride, uint32_t box_y) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return fail(ANVIL_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {x, y, z};
+  cuuint64_t strides[2] = {ystride, zstride};
+  cuuint32_t box[3] = {128, box_y, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ANVIL_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return ANVIL_OK;
+}
+
+// ------------------------------------------------------------------------------------------------- model
+
+struct Launch {
+  anvil_op op;
+  // resolved device pointers, one per op.off slot
+  void *ptr[8];
+  // GEMM tensor-core path
+  bool tc = false;
+  int bn = 0;
+  CUtensorMap mapA, mapB;
+  GemmParams gp;
+};
+
+struct anvil_model {
+  int device = 0;
+  int sms = 148;
+  cudaStream_t stream = nullptr;
+  void *consts = nullptr;
+  uint64_t const_bytes = 0;
+  void *arena = nullptr;
+  uint64_t arena_bytes = 0;
+  uint32_t *flags = nullptr;         // FLAG_WORDS device words
+  std::vector<Launch> launches;
+  cudaGraphExec_t graph = nullptr;
+  std::vector<cudaEvent_t> events;
+};
+
+extern "C" int anvil_device_count(int *count) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  if (count) *count = n;
+  return ANVIL_OK;
+}
+
+extern "C" int anvil_cuda_init(int device) {
+  int n = 0;
+  anvil_device_count(&n);
+  if (device < 0 || device >= n) return fail(ANVIL_E_UNSUPPORTED, "device %d not available (%d visible)", device, n);
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10)
+    return fail(ANVIL_E_UNSUPPORTED, "device %d is sm_%d%d; libanvil_cuda is built for sm_100a (B200)", device,
+                prop.major, prop.minor);
+  CK(cudaSetDevice(device));
+  return ANVIL_OK;
+}
+
+template <typename K>
+static int set_smem(K kernel, int bytes) {
+  CK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  return ANVIL_OK;
+}
+
+extern "C" int anvil_model_create(int device, const void *consts, uint64_t const_bytes, anvil_model **out) {
+  if (!out) return fail(ANVIL_E_BAD_ARG, "out is NULL");
+  *out = nullptr;
+  int rc = anvil_cuda_init(device);
+  if (rc) return rc;
+  anvil_model *m = new anvil_model();
+  m->device = device;
+  cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, device);
+  auto cleanup = [&](int code) {
+    anvil_model_free(m);
+    return code;
+  };
+  if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
+    return cleanup(fail(ANVIL_E_CUDA, "cudaStreamCreate failed"));
+  if (cudaMalloc(&m->flags, FLAG_WORDS * sizeof(uint32_t)) != cudaSuccess)
+    return cleanup(fail(ANVIL_E_OOM, "cannot allocate the flag words"));
+  if (const_bytes) {
+    if (!consts) return cleanup(fail(ANVIL_E_BAD_ARG, "consts is NULL with const_bytes = %llu",
+                                     (unsigned long long)const_bytes));
+    if (cudaMalloc(&m->consts, const_bytes) != cudaSuccess)
+      return cleanup(fail(ANVIL_E_OOM, "cannot allocate %llu const bytes", (unsigned long long)const_bytes));
+    if (cudaMemcpy(m->consts, consts, const_bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+      return cleanup(fail(ANVIL_E_CUDA, "const upload failed"));
+  }
+  m->const_bytes = const_bytes;
+  static bool attrs = false;       // per process: the attribute is per function, valid on every device
+  if (!attrs) {
+    int r = 0;
+    r |= set_smem(qgemm_tc_kernel<64, 1>, TcCfg<64>::SMEM_BYTES);
+    r |= set_smem(qgemm_tc_kernel<64, 2>, TcCfg<64>::SMEM_BYTES);
+    r |= set_smem(qgemm_tc_kernel<128, 1>, TcCfg<128>::SMEM_BYTES);
+    r |= set_smem(qgemm_tc_kernel<128, 2>, TcCfg<128>::SMEM_BYTES);
+    r |= set_smem(qgemm_tc_kernel<256, 1>, TcCfg<256>::SMEM_BYTES);
+    r |= set_smem(qgemm_tc_kernel<256, 2>, TcCfg<256>::SMEM_BYTES);
+    if (r) return cleanup(ANVIL_E_CUDA);
+    attrs = true;
+  }
+  *out = m;
+  return ANVIL_OK;
+}
+
+extern "C" void anvil_model_free(anvil_model *m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  if (m->graph) cudaGraphExecDestroy(m->graph);
+  for (auto e : m->events) cudaEventDestroy(e);
+  if (m->arena) cudaFree(m->arena);
+  if (m->consts) cudaFree(m->consts);
+  if (m->flags) cudaFree(m->flags);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+// Resolve a location to a device pointer, checking [off, off + bytes) against its region.
+static int resolve(anvil_model *m, const anvil_op &op, int slot, uint64_t bytes, void **ptr, bool required = true) {
+  uint64_t loc = op.off[slot];
+  if (loc == ANVIL_LOC_NONE) {
+    *ptr = nullptr;
+    if (required) return fail(ANVIL_E_BAD_ARG, "op %d (kind %d): operand slot %d is missing", op.op_index, op.kind, slot);
+    return ANVIL_OK;
+  }
+  bool is_const = (loc & ANVIL_LOC_CONST) != 0;
+  uint64_t off = loc & ~ANVIL_LOC_CONST;
+  uint64_t size = is_const ? m->const_bytes : m->arena_bytes;
+  if (off > size || bytes > size - off)
+    return fail(ANVIL_E_BAD_ARG, "op %d (kind %d): slot %d range [%llu, %llu) outside the %s region (%llu bytes)",
+                op.op_index, op.kind, slot, (unsigned long long)off, (unsigned long long)(off + bytes),
+                is_const ? "const" : "arena", (unsigned long long)size);
+  *ptr = static_cast<uint8_t *>(is_const ? m->consts : m->arena) + off;
+  return ANVIL_OK;
+}
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+static int prepare_gemm(anvil_model *m, Launch &L) {
+  const anvil_op &op = L.op;
+  const int64_t batch = op.dims[0], M = op.dims[1], N = op.dims[2], K = op.dims[3];
+  const int64_t a_bs = op.strides[0], bt_bs = op.strides[1], o_bs = op.strides[2], o_rs = op.strides[3];
+  if (batch < 1 || M < 1 || N < 1 || K < 1) return fail(ANVIL_E_BAD_ARG, "op %d: bad gemm dims", op.op_index);
+  if (op.out_bytes != 1 && op.out_bytes != 2) return fail(ANVIL_E_BAD_ARG, "op %d: gemm output must be i8 or i16", op.op_index);
+  if (op.shift < 0 || op.shift > 31) return fail(ANVIL_E_BAD_ARG, "op %d: shift %lld outside [0, 31]", op.op_index, (long long)op.shift);
+  if (a_bs < 0 || bt_bs < 0 || o_bs < 0 || o_rs < N) return fail(ANVIL_E_BAD_ARG, "op %d: bad gemm strides", op.op_index);
+  int rc;
+  const uint64_t a_bytes = (uint64_t)((batch - 1) * a_bs + M * K);
+  const uint64_t b_bytes = (uint64_t)((bt_bs ? (batch - 1) * bt_bs : 0) + N * K);
+  const uint64_t o_bytes = (uint64_t)(((batch - 1) * o_bs + (M - 1) * o_rs + N) * op.out_bytes);
+  if ((rc = resolve(m, op, 0, a_bytes, &L.ptr[0]))) return rc;
+  if ((rc = resolve(m, op, 1, b_bytes, &L.ptr[1]))) return rc;
+  if ((rc = resolve(m, op, 2, o_bytes, &L.ptr[2]))) return rc;
+  if ((rc = resolve(m, op, 3, 256, &L.ptr[3], (op.flags & ANVIL_F_LUT) != 0))) return rc;
+  if ((rc = resolve(m, op, 4, (uint64_t)N * 4, &L.ptr[4], (op.flags & ANVIL_F_BIAS) != 0))) return rc;
+  GemmParams &p = L.gp;
+  memset(&p, 0, sizeof p);
+  p.batch = batch; p.M = M; p.N = N; p.K = K;
+  p.a_bstride = a_bs; p.bt_bstride = bt_bs; p.o_bstride = o_bs; p.o_rstride = o_rs;
+  p.A = (const int8_t *)L.ptr[0];
+  p.BT = (const int8_t *)L.ptr[1];
+  p.out = L.ptr[2];
+  p.lut = (op.flags & ANVIL_F_LUT) ? (const int8_t *)L.ptr[3] : nullptr;
+  p.bias = (op.flags & ANVIL_F_BIAS) ? (const int32_t *)L.ptr[4] : nullptr;
+  p.mult = op.mult;
+  p.shift = (int)op.shift;
+  p.out_bytes = op.out_bytes;
+  p.check = (op.flags & ANVIL_F_CHECKED) ? 1 : 0;
+  p.flags = m->flags;
+  p.op_index = op.op_index;
+  const bool tc_ok = !(op.flags & ANVIL_F_SIMT) && K % 16 == 0 && a_bs % 16 == 0 && bt_bs % 16 == 0 &&
+                     aligned16(p.A) && aligned16(p.BT) && M <= (1ll << 31) - 256 && N <= (1ll << 31) - 256 &&
+                     batch <= (1ll << 31) - 1;
+  L.tc = tc_ok;
+  if (!tc_ok) return ANVIL_OK;
+  L.bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
+  p.m_tiles = (M + TC_BM - 1) / TC_BM;
+  p.n_tiles = (N + L.bn - 1) / L.bn;
+  p.tiles = batch * p.m_tiles * p.n_tiles;
+  const uint64_t a_z = batch, a_zs = a_bs ? a_bs : M * K;
+  const uint64_t b_z = bt_bs ? batch : 1, b_zs = bt_bs ? bt_bs : N * K;
+  if ((rc = make_map_i8(&L.mapA, p.A, K, M, a_z, K, a_zs, TC_BM))) return rc;
+  if ((rc = make_map_i8(&L.mapB, p.BT, K, N, b_z, K, b_zs, L.bn))) return rc;
+  return ANVIL_OK;
+}
+
+static int prepare_op(anvil_model *m, Launch &L) {
+  const anvil_op &op = L.op;
+  int rc;
+  const int64_t *d = op.dims;
+  switch (op.kind) {
+    case ANVIL_OP_GEMM:
+      return prepare_gemm(m, L);
+    case ANVIL_OP_LUT:
+      if ((rc = resolve(m, op, 0, d[0], &L.ptr[0]))) return rc;
+      if ((rc = resolve(m, op, 1, 256, &L.ptr[1]))) return rc;
+      return resolve(m, op, 2, d[0], &L.ptr[2]);
+    case ANVIL_OP_LUT_MUL:
+      if ((rc = resolve(m, op, 0, d[0], &L.ptr[0]))) return rc;
+      if ((rc = resolve(m, op, 1, d[0], &L.ptr[1]))) return rc;
+      if ((rc = resolve(m, op, 2, 256, &L.ptr[2]))) return rc;
+      return resolve(m, op, 3, d[0], &L.ptr[3]);
+    case ANVIL_OP_ADD_REQUANT:
+      if ((op.in_bytes != 1 && op.in_bytes != 2) || (op.in2_bytes != 1 && op.in2_bytes != 2) ||
+          (op.out_bytes != 1 && op.out_bytes != 2))
+        return fail(ANVIL_E_BAD_ARG, "op %d: add_requant operands must be i8 or i16", op.op_index);
+      if ((rc = resolve(m, op, 0, d[0] * op.in_bytes, &L.ptr[0]))) return rc;
+      if ((rc = resolve(m, op, 1, d[0] * op.in2_bytes, &L.ptr[1]))) return rc;
+      return resolve(m, op, 2, d[0] * op.out_bytes, &L.ptr[2]);
+    case ANVIL_OP_NORM:
+      if (op.in_bytes != 1 && op.in_bytes != 2) return fail(ANVIL_E_BAD_ARG, "op %d: norm input must be i8 or i16", op.op_index);
+      if (d[1] < 1 || d[2] < 1) return fail(ANVIL_E_BAD_ARG, "op %d: bad norm dims", op.op_index);
+      if ((rc = resolve(m, op, 0, d[0] * d[1] * op.in_bytes, &L.ptr[0]))) return rc;
+      if ((rc = resolve(m, op, 1, d[1], &L.ptr[1]))) return rc;
+      if ((rc = resolve(m, op, 2, d[2] * 4, &L.ptr[2]))) return rc;
+      if ((rc = resolve(m, op, 3, d[0] * d[1], &L.ptr[3]))) return rc;
+      return resolve(m, op, 4, d[1], &L.ptr[4], (op.flags & ANVIL_F_BIAS) != 0);
+    case ANVIL_OP_SOFTMAX:
+      if (op.out_bytes != 1 && op.out_bytes != 4) return fail(ANVIL_E_BAD_ARG, "op %d: softmax output must be i8 or i32", op.op_index);
+      if ((rc = resolve(m, op, 0, d[0] * d[1] * d[2], &L.ptr[0]))) return rc;
+      if ((rc = resolve(m, op, 1, 256 * 4, &L.ptr[1]))) return rc;
+      return resolve(m, op, 2, d[0] * d[1] * d[2] * op.out_bytes, &L.ptr[2]);
+    case ANVIL_OP_TRANSPOSE: {
+      const int rank = (int)d[0];
+      if (rank < 1 || rank > 6 || (op.in_bytes != 1 && op.in_bytes != 2 && op.in_bytes != 4))
+        return fail(ANVIL_E_BAD_ARG, "op %d: bad transpose rank/element size", op.op_index);
+      int64_t total = 1, span = 0;
+      for (int i = 0; i < rank; ++i) {
+        if (d[1 + i] < 1 || op.strides[i] < 0) return fail(ANVIL_E_BAD_ARG, "op %d: bad transpose dims", op.op_index);
+        total *= d[1 + i];
+        span += (d[1 + i] - 1) * op.strides[i];
+      }
+      if ((rc = resolve(m, op, 0, (span + 1) * op.in_bytes, &L.ptr[0]))) return rc;
+      return resolve(m, op, 1, total * op.in_bytes, &L.ptr[1]);
+    }
+    case ANVIL_OP_EMBED:
+      if ((rc = resolve(m, op, 0, d[0] * d[1] * 4, &L.ptr[0]))) return rc;
+      if ((rc = resolve(m, op, 1, d[3] * d[2], &L.ptr[1]))) return rc;
+      if ((rc = resolve(m, op, 2, d[1] * d[2], &L.ptr[2]))) return rc;
+      return resolve(m, op, 3, d[0] * d[1] * d[2], &L.ptr[3]);
+    case ANVIL_OP_COPY:
+      if ((rc = resolve(m, op, 0, d[0], &L.ptr[0]))) return rc;
+      return resolve(m, op, 1, d[0], &L.ptr[1]);
+    default:
+      return fail(ANVIL_E_UNSUPPORTED, "op %d: unknown kind %d", op.op_index, op.kind);
+  }
+}
+
+extern "C" int anvil_model_prepare(anvil_model *m, const anvil_op *ops, int n_ops, uint64_t arena_bytes) {
+  if (!m || (n_ops && !ops) || n_ops < 0) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_prepare");
+  CK(cudaSetDevice(m->device));
+  CK(cudaStreamSynchronize(m->stream));
+  if (m->graph) {
+    cudaGraphExecDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  if (arena_bytes > m->arena_bytes) {
+    if (m->arena) cudaFree(m->arena);
+    m->arena = nullptr;
+    m->arena_bytes = 0;
+    if (cudaMalloc(&m->arena, arena_bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(ANVIL_E_OOM, "cannot allocate a %llu-byte activation arena", (unsigned long long)arena_bytes);
+    }
+    m->arena_bytes = arena_bytes;
+  }
+  std::vector<Launch> ls(n_ops);
+  for (int i = 0; i < n_ops; ++i) {
+    ls[i].op = ops[i];
+    for (int s = 0; s < 8; ++s) ls[i].ptr[s] = nullptr;
+    int rc = prepare_op(m, ls[i]);
+    if (rc) return rc;
+  }
+  m->launches.swap(ls);
+  for (auto e : m->events) cudaEventDestroy(e);
+  m->events.clear();
+  return ANVIL_OK;
+}
+
+static int grid_for(anvil_model *m, int64_t work, int per_block, int max_waves = 8) {
+  int64_t g = (work + per_block - 1) / per_block;
+  int64_t cap = (int64_t)m->sms * max_waves;
+  if (g > cap) g = cap;
+  return (int)std::max<int64_t>(1, g);
+}
+
+static int launch_op(anvil_model *m, Launch &L) {
+  const anvil_op &op = L.op;
+  const int64_t *d = op.dims;
+  cudaStream_t st = m->stream;
+  const bool chk = (op.flags & ANVIL_F_CHECKED) != 0;
+  uint32_t *fl = m->flags;
+  const int oi = op.op_index;
+  switch (op.kind) {
+    case ANVIL_OP_GEMM: {
+      GemmParams &p = L.gp;
+      if (L.tc) {
+        const int grid = (int)std::min<int64_t>(p.tiles, m->sms);
+#define TC_LAUNCH(BN, OB) qgemm_tc_kernel<BN, OB><<<grid, TC_THREADS, TcCfg<BN>::SMEM_BYTES, st>>>(L.mapA, L.mapB, p)
+        if (L.bn == 64) { if (op.out_bytes == 1) TC_LAUNCH(64, 1); else TC_LAUNCH(64, 2); }
+        else if (L.bn == 128) { if (op.out_bytes == 1) TC_LAUNCH(128, 1); else TC_LAUNCH(128, 2); }
+        else { if (op.out_bytes == 1) TC_LAUNCH(256, 1); else TC_LAUNCH(256, 2); }
+#undef TC_LAUNCH
+      } else {
+        dim3 grid((unsigned)((p.N + 63) / 64), (unsigned)((p.M + 63) / 64), (unsigned)p.batch);
+        if (grid.y > 65535 || grid.z > 65535) return fail(ANVIL_E_BAD_ARG, "op %d: gemm too large for the SIMT path", oi);
+        if (chk) qgemm_simt_kernel<true><<<grid, 256, 0, st>>>(p);
+        else qgemm_simt_kernel<false><<<grid, 256, 0, st>>>(p);
+      }
+      break;
+    }
+    case ANVIL_OP_LUT:
+      lut_kernel<<<grid_for(m, d[0], 256 * 16), 256, 0, st>>>((const int8_t *)L.ptr[0], (const int8_t *)L.ptr[1],
+                                                            (int8_t *)L.ptr[2], d[0]);
+      break;
+    case ANVIL_OP_LUT_MUL: {
+      auto k = chk ? lut_mul_kernel<true> : lut_mul_kernel<false>;
+      k<<<grid_for(m, d[0], 256 * 4), 256, 0, st>>>((const int8_t *)L.ptr[0], (const int8_t *)L.ptr[1],
+                                                   (const int8_t *)L.ptr[2], (int8_t *)L.ptr[3], d[0], op.mult,
+                                                   (int)op.shift, fl, oi);
+      break;
+    }
+    case ANVIL_OP_ADD_REQUANT: {
+      const int code = (op.in_bytes - 1) * 4 + (op.in2_bytes - 1) * 2 + (op.out_bytes - 1) + (chk ? 8 : 0);
+      void (*k)(const void *, const void *, void *, int64_t, long long, long long, int, uint32_t *, int) = nullptr;
+      switch (code) {
+#define AR(C, A, B, O, CH) case C: k = add_requant_kernel<A, B, O, CH>; break;
+        AR(0, 1, 1, 1, false) AR(1, 1, 1, 2, false) AR(2, 1, 2, 1, false) AR(3, 1, 2, 2, false)
+        AR(4, 2, 1, 1, false) AR(5, 2, 1, 2, false) AR(6, 2, 2, 1, false) AR(7, 2, 2, 2, false)
+        AR(8, 1, 1, 1, true) AR(9, 1, 1, 2, true) AR(10, 1, 2, 1, true) AR(11, 1, 2, 2, true)
+        AR(12, 2, 1, 1, true) AR(13, 2, 1, 2, true) AR(14, 2, 2, 1, true) AR(15, 2, 2, 2, true)
+#undef AR
+      }
+      k<<<grid_for(m, d[0], 256 * 8), 256, 0, st>>>(L.ptr[0], L.ptr[1], L.ptr[2], d[0], op.ma, op.mb, (int)op.shift,
+                                                   fl, oi);
+      break;
+    }
+    case ANVIL_OP_NORM: {
+      auto k = op.in_bytes == 1 ? (chk ? norm_kernel<1, true> : norm_kernel<1, false>)
+                                : (chk ? norm_kernel<2, true> : norm_kernel<2, false>);
+      k<<<grid_for(m, d[0], 8), 256, 0, st>>>(L.ptr[0], (const int8_t *)L.ptr[1], (const int32_t *)L.ptr[2],
+                                             (const int8_t *)L.ptr[4], (int8_t *)L.ptr[3], d[0], (int)d[1], (int)d[2],
+                                             op.mult, (int)op.shift, (int)op.ss_shift, op.ss_init,
+                                             (op.flags & ANVIL_F_CENTER) ? 1 : 0, fl, oi);
+      break;
+    }
+    case ANVIL_OP_SOFTMAX: {
+      const int64_t rows = d[0] * d[1];
+      auto k = op.out_bytes == 1 ? (chk ? softmax_kernel<1, true> : softmax_kernel<1, false>)
+                                 : (chk ? softmax_kernel<4, true> : softmax_kernel<4, false>);
+      k<<<grid_for(m, rows, 8), 256, 0, st>>>((const int8_t *)L.ptr[0], (const int32_t *)L.ptr[1], L.ptr[2], rows,
+                                             (int)d[1], (int)d[2], op.one, (op.flags & ANVIL_F_CAUSAL) ? 1 : 0, fl,
+                                             oi);
+      break;
+    }
+    case ANVIL_OP_TRANSPOSE: {
+      TransposeDims td;
+      td.rank = (int)d[0];
+      int64_t total = 1;
+      for (int i = 0; i < 6; ++i) {
+        td.n[i] = i < td.rank ? d[1 + i] : 1;
+        td.st[i] = i < td.rank ? op.strides[i] : 0;
+        total *= td.n[i];
+      }
+      const int g = grid_for(m, total, 256);
+      if (op.in_bytes == 1) transpose_kernel<1><<<g, 256, 0, st>>>(L.ptr[0], L.ptr[1], td, total);
+      else if (op.in_bytes == 2) transpose_kernel<2><<<g, 256, 0, st>>>(L.ptr[0], L.ptr[1], td, total);
+      else transpose_kernel<4><<<g, 256, 0, st>>>(L.ptr[0], L.ptr[1], td, total);
+      break;
+    }
+    case ANVIL_OP_EMBED: {
+      auto k = chk ? embed_kernel<true> : embed_kernel<false>;
+      const int64_t rows = d[0] * d[1];
+      k<<<grid_for(m, rows, 8), 256, 0, st>>>((const int32_t *)L.ptr[0], (const int8_t *)L.ptr[1],
+                                             (const int8_t *)L.ptr[2], (int8_t *)L.ptr[3], rows, (int)d[1], (int)d[2],
+                                             d[3], op.ma, op.mb, (int)op.shift, fl, oi);
+      break;
+    }
+    case ANVIL_OP_COPY:
+      CK(cudaMemcpyAsync(L.ptr[1], L.ptr[0], d[0], cudaMemcpyDeviceToDevice, st));
+      break;
+    default:
+      return fail(ANVIL_E_UNSUPPORTED, "op %d: unknown kind %d", oi, op.kind);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(ANVIL_E_CUDA, "op %d (kind %d) launch failed: %s", oi, op.kind, cudaGetErrorString(e));
+  return ANVIL_OK;
+}
+
+static int check_flags(anvil_model *m, const uint32_t *h) {
+  if (h[FLAG_TIMEOUT])
+    return fail(ANVIL_E_TIMEOUT, "op %u: a device wait timed out", h[FLAG_TIMEOUT] - 1);
+  if (h[FLAG_OVERFLOW])
+    return fail(ANVIL_E_OVERFLOW, "op %u: an int32 intermediate left int32", h[FLAG_OVERFLOW] - 1);
+  if (h[FLAG_INDEX])
+    return fail(ANVIL_E_INDEX, "op %u: an index left its table", h[FLAG_INDEX] - 1);
+  return ANVIL_OK;
+}
+
+extern "C" int anvil_model_run(anvil_model *m, const anvil_io *inputs, int n_inputs, const anvil_io *outputs,
+                               int n_outputs, float *kernel_us) {
+  if (!m) return fail(ANVIL_E_BAD_ARG, "model is NULL");
+  CK(cudaSetDevice(m->device));
+  cudaStream_t st = m->stream;
+  for (int i = 0; i < n_inputs; ++i) {
+    const anvil_io &io = inputs[i];
+    if (io.offset > m->arena_bytes || io.bytes > m->arena_bytes - io.offset)
+      return fail(ANVIL_E_BAD_ARG, "input %d: [%llu, +%llu) outside the arena", i, (unsigned long long)io.offset,
+                  (unsigned long long)io.bytes);
+    CK(cudaMemcpyAsync(static_cast<uint8_t *>(m->arena) + io.offset, io.host, io.bytes, cudaMemcpyHostToDevice, st));
+  }
+  CK(cudaMemsetAsync(m->flags, 0, FLAG_WORDS * sizeof(uint32_t), st));
+  const int n = (int)m->launches.size();
+  if (kernel_us && (int)m->events.size() < n + 1) {
+    for (auto e : m->events) cudaEventDestroy(e);
+    m->events.assign(n + 1, nullptr);
+    for (auto &e : m->events) CK(cudaEventCreate(&e));
+  }
+  if (kernel_us) CK(cudaEventRecord(m->events[0], st));
+  for (int i = 0; i < n; ++i) {
+    int rc = launch_op(m, m->launches[i]);
+    if (rc) return rc;
+    if (kernel_us) CK(cudaEventRecord(m->events[i + 1], st));
+  }
+  uint32_t hflags[FLAG_WORDS];
+  CK(cudaMemcpyAsync(hflags, m->flags, sizeof hflags, cudaMemcpyDeviceToHost, st));
+  for (int i = 0; i < n_outputs; ++i) {
+    const anvil_io &io = outputs[i];
+    if (io.offset > m->arena_bytes || io.bytes > m->arena_bytes - io.offset)
+      return fail(ANVIL_E_BAD_ARG, "output %d: [%llu, +%llu) outside the arena", i, (unsigned long long)io.offset,
+                  (unsigned long long)io.bytes);
+    CK(cudaMemcpyAsync(io.host, static_cast<uint8_t *>(m->arena) + io.offset, io.bytes, cudaMemcpyDeviceToHost, st));
+  }
+  CK(cudaStreamSynchronize(st));
+  if (kernel_us)
+    for (int i = 0; i < n; ++i) {
+      float ms = 0;
+      CK(cudaEventElapsedTime(&ms, m->events[i], m->events[i + 1]));
+      kernel_us[i] = ms * 1000.0f;
+    }
+  return check_flags(m, hflags);
+}
+
+extern "C" int anvil_model_run_device(anvil_model *m, int iters, int use_graph, float *ms) {
+  if (!m || iters < 1) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_run_device");
+  CK(cudaSetDevice(m->device));
+  cudaStream_t st = m->stream;
+  if (use_graph && !m->graph) {
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    int rc = ANVIL_OK;
+    for (auto &L : m->launches)
+      if ((rc = launch_op(m, L))) break;
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (rc) return rc;
+    if (e != cudaSuccess) return fail(ANVIL_E_CUDA, "graph capture failed: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&m->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(ANVIL_E_CUDA, "graph instantiate failed: %s", cudaGetErrorString(e));
+  }
+  cudaEvent_t e0, e1;
+  CK(cudaEventCreate(&e0));
+  CK(cudaEventCreate(&e1));
+  CK(cudaMemsetAsync(m->flags, 0, FLAG_WORDS * sizeof(uint32_t), st));
+  CK(cudaEventRecord(e0, st));
+  for (int it = 0; it < iters; ++it) {
+    if (use_graph) {
+      CK(cudaGraphLaunch(m->graph, st));
+    } else {
+      for (auto &L : m->launches) {
+        int rc = launch_op(m, L);
+        if (rc) return rc;
+      }
+    }
+  }
+  CK(cudaEventRecord(e1, st));
+  uint32_t hflags[FLAG_WORDS];
+  CK(cudaMemcpyAsync(hflags, m->flags, sizeof hflags, cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  float t = 0;
+  CK(cudaEventElapsedTime(&t, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (ms) *ms = t;
+  return check_flags(m, hflags);
+}
+
+extern "C" int anvil_model_read(anvil_model *m, uint64_t offset, void *host, uint64_t bytes) {
+  if (!m || !host) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_read");
+  if (offset > m->arena_bytes || bytes > m->arena_bytes - offset) return fail(ANVIL_E_BAD_ARG, "read outside the arena");
+  CK(cudaSetDevice(m->device));
+  CK(cudaMemcpyAsync(host, static_cast<uint8_t *>(m->arena) + offset, bytes, cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  return ANVIL_OK;
+}
+
+extern "C" int anvil_model_write(anvil_model *m, uint64_t offset, const void *host, uint64_t bytes) {
+  if (!m || !host) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_write");
+  if (offset > m->arena_bytes || bytes > m->arena_bytes - offset) return fail(ANVIL_E_BAD_ARG, "write outside the arena");
+  CK(cudaSetDevice(m->device));
+  CK(cudaMemcpyAsync(static_cast<uint8_t *>(m->arena) + offset, host, bytes, cudaMemcpyHostToDevice, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  return ANVIL_OK;
+}
+
+extern "C" int anvil_model_arena(anvil_model *m, uint64_t *arena_ptr, uint64_t *const_ptr) {
+  if (!m) return fail(ANVIL_E_BAD_ARG, "model is NULL");
+  if (arena_ptr) *arena_ptr = reinterpret_cast<uint64_t>(m->arena);
+  if (const_ptr) *const_ptr = reinterpret_cast<uint64_t>(m->consts);
+  return ANVIL_OK;
+}
+
+// ------------------------------------------------------------------------------------- standalone GEMM
+
+extern "C" int anvil_gemm_requant(const int8_t *A, const int8_t *BT, int8_t *out, int64_t M, int64_t N, int64_t K,
+                                  int32_t mult, int32_t shift, uint32_t flags, void *stream) {
+  if (!A || !BT || !out || M < 1 || N < 1 || K < 1 || shift < 0 || shift > 31)
+    return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_gemm_requant");
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  static thread_local anvil_model *scratch[64] = {};
+  if (dev >= 64) return fail(ANVIL_E_BAD_ARG, "device %d out of range", dev);
+  if (!scratch[dev]) {
+    int rc = anvil_model_create(dev, nullptr, 0, &scratch[dev]);
+    if (rc) return rc;
+  }
+  anvil_model *m = scratch[dev];
+  Launch L;
+  memset(&L.op, 0, sizeof L.op);
+  L.op.kind = ANVIL_OP_GEMM;
+  L.op.flags = flags & (ANVIL_F_CHECKED | ANVIL_F_SIMT);
+  L.op.out_bytes = 1;
+  L.op.dims[0] = 1; L.op.dims[1] = M; L.op.dims[2] = N; L.op.dims[3] = K;
+  L.op.strides[0] = 0; L.op.strides[1] = 0; L.op.strides[2] = 0; L.op.strides[3] = N;
+  L.op.mult = mult;
+  L.op.shift = shift;
+  for (int s = 0; s < 8; ++s) L.op.off[s] = ANVIL_LOC_NONE;
+  // bypass region resolution: caller-owned device pointers
+  GemmParams &p = L.gp;
+  memset(&p, 0, sizeof p);
+  p.batch = 1; p.M = M; p.N = N; p.K = K;
+  p.o_rstride = N;
+  p.A = A; p.BT = BT; p.out = out;
+  p.mult = mult; p.shift = shift; p.out_bytes = 1;
+  p.check = (flags & ANVIL_F_CHECKED) ? 1 : 0;
+  p.flags = m->flags;
+  L.tc = !(flags & ANVIL_F_SIMT) && K % 16 == 0 && aligned16(A) && aligned16(BT);
+  if (L.tc) {
+    L.bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
+    p.m_tiles = (M + TC_BM - 1) / TC_BM;
+    p.n_tiles = (N + L.bn - 1) / L.bn;
+    p.tiles = p.m_tiles * p.n_tiles;
+    int rc;
+    if ((rc = make_map_i8(&L.mapA, A, K, M, 1, K, M * K, TC_BM))) return rc;
+    if ((rc = make_map_i8(&L.mapB, BT, K, N, 1, K, N * K, L.bn))) return rc;
+  }
+  cudaStream_t saved = m->stream;
+  m->stream = static_cast<cudaStream_t>(stream);
+  if (p.check) CK(cudaMemsetAsync(m->flags, 0, FLAG_WORDS * sizeof(uint32_t), m->stream));
+  int rc = launch_op(m, L);
+  m->stream = saved;
+  if (rc) return rc;
+  if (p.check) {
+    uint32_t h[FLAG_WORDS];
+    CK(cudaMemcpyAsync(h, m->flags, sizeof h, cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)));
+    CK(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    return check_flags(m, h);
+  }
+  return ANVIL_OK;
+}

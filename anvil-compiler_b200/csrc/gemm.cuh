@@ -1,0 +1,310 @@
+// int8 x int8 -> int32 GEMMs with the exact requant epilogue (qmatmul / qlinear, anvil/semantics.py:95-103):
+//   out[b, i, j] = [lut[. + 128] o] clamp_dtype(((sum_k A[b,i,k] * BT[b,j,k] + bias[j]) * M + 2^(s-1)) >> s)
+//
+// qgemm_tc:   the sm_100a path. Persistent, warp-specialised: warp 0 issues TMA tile loads (128-byte swizzle)
+//             into a STAGES-deep shared-memory ring, warp 1 issues tcgen05.mma kind::i8 (M = 128, N = BN, K = 32
+//             per instruction) into one of two TMEM accumulators, warps 2-5 drain the other accumulator with
+//             tcgen05.ld and run the requant epilogue, so the epilogue of tile i overlaps the MMAs of tile i+1.
+// qgemm_simt: CUDA-core fallback for shapes the TMA path cannot address (K or strides not a multiple of 16
+//             bytes) and for tiny problems where launch latency dominates.
+//
+// int32 accumulation wraps mod 2^32, so it is exact whenever the final sum fits int32 (the contract the oracle
+// checks); CHECK re-checks acc, acc + bias, acc*M and acc*M + round against int32 on the device.
+#pragma once
+
+#include "common.cuh"
+
+namespace anvil {
+
+struct GemmParams {
+  int64_t batch, M, N, K;
+  int64_t a_bstride, bt_bstride;       // elements between batches (bt 0 = one weight for every batch)
+  int64_t o_bstride, o_rstride;        // output elements between batches / rows
+  const int8_t *A;
+  const int8_t *BT;
+  void *out;
+  const int8_t *lut;                   // nullptr: no LUT epilogue
+  const int32_t *bias;                 // nullptr: no bias
+  long long mult;
+  int shift;
+  int out_bytes;                       // 1 (i8) or 2 (i16)
+  int check;
+  uint32_t *flags;
+  int op_index;
+  int64_t m_tiles, n_tiles, tiles;     // tc path tiling
+};
+
+// One output element from its int32 accumulator (shared by both kernels).
+template <bool CHECK>
+__device__ __forceinline__ int gemm_epi(int32_t acc, int32_t bias, const GemmParams &p, const int8_t *lut_s,
+                                        int lo, int hi, bool &bad) {
+  long long a = acc;
+  if (p.bias) {
+    a += bias;
+    if (CHECK) bad |= !fits_i32(a);
+  }
+  int v = requant64<CHECK>(a, p.mult, p.shift, lo, hi, bad);
+  if (lut_s) v = lut_s[v + 128];
+  return v;
+}
+
+// ------------------------------------------------------------------------------------------------------ SIMT
+// 64 x 64 output tile per 256-thread block, 4 x 4 per thread, K staged through shared memory 32 at a time.
+template <bool CHECK>
+__global__ void __launch_bounds__(256) qgemm_simt_kernel(GemmParams p) {
+  __shared__ int32_t As[32][65];
+  __shared__ int32_t Bs[32][65];
+  __shared__ int8_t lut_s[256];
+  const int tid = threadIdx.x;
+  if (p.lut)
+    for (int i = tid; i < 256; i += 256) lut_s[i] = p.lut[i];
+  const int64_t b = blockIdx.z;
+  const int64_t i0 = blockIdx.y * 64, j0 = blockIdx.x * 64;
+  const int8_t *A = p.A + b * p.a_bstride;
+  const int8_t *BT = p.BT + b * p.bt_bstride;
+  const int tx = tid & 15, ty = tid >> 4;
+  int32_t acc[4][4] = {};
+  for (int64_t k0 = 0; k0 < p.K; k0 += 32) {
+    for (int e = tid; e < 64 * 32; e += 256) {
+      int r = e / 32, kk = e % 32;
+      int64_t gi = i0 + r, gj = j0 + r, gk = k0 + kk;
+      As[kk][r] = (gi < p.M && gk < p.K) ? (int32_t)A[gi * p.K + gk] : 0;
+      Bs[kk][r] = (gj < p.N && gk < p.K) ? (int32_t)BT[gj * p.K + gk] : 0;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < 32; ++kk) {
+      int32_t av[4], bv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        av[q] = As[kk][ty + 16 * q];
+        bv[q] = Bs[kk][tx + 16 * q];
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[q][r] += av[q] * bv[r];
+    }
+    __syncthreads();
+  }
+  int lo, hi;
+  if (p.out_bytes == 1) { lo = -128; hi = 127; } else { lo = -32768; hi = 32767; }
+  bool bad = false;
+  const int8_t *lt = p.lut ? lut_s : nullptr;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    int64_t gi = i0 + ty + 16 * q;
+    if (gi >= p.M) continue;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      int64_t gj = j0 + tx + 16 * r;
+      if (gj >= p.N) continue;
+      int v = gemm_epi<CHECK>(acc[q][r], p.bias ? p.bias[gj] : 0, p, lt, lo, hi, bad);
+      int64_t o = b * p.o_bstride + gi * p.o_rstride + gj;
+      if (p.out_bytes == 1) reinterpret_cast<int8_t *>(p.out)[o] = (int8_t)v;
+      else reinterpret_cast<int16_t *>(p.out)[o] = (int16_t)v;
+    }
+  }
+  if (CHECK && __any_sync(0xffffffffu, bad) && bad) raise_flag(p.flags, FLAG_OVERFLOW, p.op_index);
+}
+
+// ---------------------------------------------------------------------------------------------- tcgen05 (TC)
+
+constexpr int TC_BM = 128;
+constexpr int TC_BK = 128;                // bytes of K per stage = one 128-byte swizzle row
+constexpr int TC_THREADS = 192;           // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int TC_SMEM_RING = 192 * 1024;  // bytes of A/B stages
+
+template <int BN>
+struct TcCfg {
+  static constexpr int A_BYTES = TC_BM * TC_BK;
+  static constexpr int B_BYTES = BN * TC_BK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = TC_SMEM_RING / STAGE_BYTES > 8 ? 8 : TC_SMEM_RING / STAGE_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;     // two accumulators
+  // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2]; then the TMEM base slot, abort word, LUT
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int MISC_OFF = BAR_OFF + (2 * STAGES + 4) * 8;
+  static constexpr int SMEM_BYTES = MISC_OFF + 16 + 256 + 1024;   // + 1 KB slack to align the ring to 1024 B
+};
+
+// Store 32 consecutive results of one output row: 16-byte vector stores when the whole chunk is in range and
+// aligned, element stores otherwise.
+template <int OB>
+__device__ __forceinline__ void store_row32(typename IntOf<OB>::T *dst, const int (&v)[32], int count) {
+  if (count == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    if (OB == 1) {
+      uint32_t w[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        w[q] = (uint32_t)(uint8_t)v[4 * q] | ((uint32_t)(uint8_t)v[4 * q + 1] << 8) |
+               ((uint32_t)(uint8_t)v[4 * q + 2] << 16) | ((uint32_t)(uint8_t)v[4 * q + 3] << 24);
+      uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+      d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+      uint32_t w[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) w[q] = (uint32_t)(uint16_t)v[2 * q] | ((uint32_t)(uint16_t)v[2 * q + 1] << 16);
+      uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) d4[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 32; ++q)
+      if (q < count) dst[q] = (typename IntOf<OB>::T)v[q];
+  }
+}
+
+template <int BN, int OB>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmParams p) {
+  using Cfg = TcCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + Cfg::BAR_OFF);
+  uint64_t *empty = full + Cfg::STAGES;
+  uint64_t *tfull = empty + Cfg::STAGES;
+  uint64_t *tempty = tfull + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Cfg::MISC_OFF);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + Cfg::MISC_OFF + 4);
+  int8_t *lut_s = reinterpret_cast<int8_t *>(smem + Cfg::MISC_OFF + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < Cfg::STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 128);
+    }
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (p.lut)
+    for (int i = threadIdx.x; i < 256; i += TC_THREADS) lut_s[i] = p.lut[i];
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = (int)((p.K + TC_BK - 1) / TC_BK);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0, armed = 0, armed_phase = 0;     // per stage: armed at least once, parity of last arm
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+        const int64_t nb = t % p.n_tiles, rest = t / p.n_tiles;
+        const int64_t mb = rest % p.m_tiles, bb = rest / p.m_tiles;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort, p.flags, p.op_index)) { ok = false; break; }
+          armed |= 1u << stage;
+          armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+          uint8_t *sa = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t *sb = sa + Cfg::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          tma_load_3d(sa, &tmA, kb * TC_BK, (int)(mb * TC_BM), (int)bb, &full[stage]);
+          tma_load_3d(sb, &tmB, kb * TC_BK, (int)(nb * BN), p.bt_bstride ? (int)bb : 0, &full[stage]);
+          if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      if (!ok) {      // aborted: let every tile load already issued land before the CTA's smem is released
+        for (int s = 0; s < Cfg::STAGES; ++s)
+          if (armed & (1u << s)) mbar_wait_ns(&full[s], (armed_phase >> s) & 1u, 10000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_i8(TC_BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t aphase = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], aphase ^ 1u, abort, p.flags, p.op_index)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort, p.flags, p.op_index)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < TC_BK / 32; ++k) {
+            mma_i8(d_tmem, sw128_kmajor_desc(sa + 32 * k), sw128_kmajor_desc(sb + 32 * k), idesc,
+                   (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+        if (++acc == 2) { acc = 0; aphase ^= 1u; }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int lane_base = 32 * (warp & 3);
+    int acc = 0;
+    uint32_t aphase = 0;
+    int lo, hi;
+    if (OB == 1) { lo = -128; hi = 127; } else { lo = -32768; hi = 32767; }
+    const int8_t *lt = p.lut ? lut_s : nullptr;
+    bool bad = false;
+    for (int64_t t = blockIdx.x; t < p.tiles; t += gridDim.x) {
+      const int64_t nb = t % p.n_tiles, rest = t / p.n_tiles;
+      const int64_t mb = rest % p.m_tiles, bb = rest / p.m_tiles;
+      if (!mbar_wait(&tfull[acc], aphase, abort, p.flags, p.op_index)) break;
+      tc_fence_after();
+      const int64_t row = mb * TC_BM + lane_base + lane;
+      const bool row_ok = row < p.M;
+      using TO = typename IntOf<OB>::T;
+      TO *orow = reinterpret_cast<TO *>(p.out) + bb * p.o_bstride + row * p.o_rstride;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        int32_t r[32];
+        __syncwarp();
+        tmem_ld32(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c0), r);
+        const int64_t col0 = nb * BN + c0;
+        if (row_ok && col0 < p.N) {
+          int v[32];
+          if (p.check) {
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              v[q] = gemm_epi<true>(r[q], (p.bias && col0 + q < p.N) ? p.bias[col0 + q] : 0, p, lt, lo, hi, bad);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              v[q] = gemm_epi<false>(r[q], (p.bias && col0 + q < p.N) ? p.bias[col0 + q] : 0, p, lt, lo, hi, bad);
+          }
+          store_row32<OB>(orow + col0, v, (int)(p.N - col0 < 32 ? p.N - col0 : 32));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; aphase ^= 1u; }
+    }
+    if (p.check && __any_sync(0xffffffffu, bad) && bad) raise_flag(p.flags, FLAG_OVERFLOW, p.op_index);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace anvil

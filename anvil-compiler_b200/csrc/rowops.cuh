@@ -1,0 +1,281 @@
+// Memory-bound kernels: lut, lut_mul, add_requant, rmsnorm_int / layernorm_int, softmax_lut, transpose, embed.
+//
+// All are grid-stride over 16-byte vectors where the data allows it (arena buffers start 256-byte aligned), hold
+// the small tables (256 x i8 LUT, 256 x i32 exp LUT) in shared memory, and reduce rows with warp shuffles. Each
+// follows the oracle's arithmetic exactly (cited per kernel); CHECK adds the int32 range checks the reference
+// raises on, reported through the model's flag words.
+#pragma once
+
+#include "common.cuh"
+
+namespace anvil {
+
+__host__ __device__ inline void dt_range(int bytes, int &lo, int &hi) {
+  if (bytes == 1) { lo = -128; hi = 127; }
+  else if (bytes == 2) { lo = -32768; hi = 32767; }
+  else { lo = (int)0x80000000; hi = 0x7fffffff; }
+}
+
+// ------------------------------------------------------------------------------------------------------ lut
+// table[x + 128] (anvil/semantics.py:87-92)
+__global__ void lut_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ table, int8_t *__restrict__ out,
+                           int64_t n) {
+  __shared__ int8_t t[256];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) t[i] = table[i];
+  __syncthreads();
+  const int64_t nv = n / 16;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += stride) {
+    uint4 in = reinterpret_cast<const uint4 *>(x)[v];
+    uint32_t w[4] = {in.x, in.y, in.z, in.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t o = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        int xv = (int8_t)((w[q] >> (8 * b)) & 0xff);
+        o |= ((uint32_t)(uint8_t)t[xv + 128]) << (8 * b);
+      }
+      w[q] = o;
+    }
+    reinterpret_cast<uint4 *>(out)[v] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  for (int64_t i = nv * 16 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    out[i] = t[x[i] + 128];
+}
+
+// ------------------------------------------------------------------------------------------------- lut_mul
+// requant(table[x + 128] * y, M, s) (golden.swiglu_lut; anvil/lower/graph_to_tensor.py:297-300)
+template <bool CHECK>
+__global__ void lut_mul_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ y,
+                               const int8_t *__restrict__ table, int8_t *__restrict__ out, int64_t n, long long m,
+                               int s, uint32_t *flags, int op_index) {
+  __shared__ int8_t t[256];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) t[i] = table[i];
+  __syncthreads();
+  bool bad = false;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    long long prod = (long long)t[x[i] + 128] * (long long)y[i];
+    out[i] = (int8_t)requant64<CHECK>(prod, m, s, -128, 127, bad);
+  }
+  if (CHECK && __any_sync(0xffffffffu, bad) && bad) raise_flag(flags, FLAG_OVERFLOW, op_index);
+}
+
+// --------------------------------------------------------------------------------------------- add_requant
+// clamp((a*Ma + b*Mb + 2^(s-1)) >> s) to the result dtype (anvil/semantics.py:106-115; residual_add for i8)
+template <int AB, int BB, int OB, bool CHECK>
+__global__ void add_requant_kernel(const void *__restrict__ a_, const void *__restrict__ b_, void *__restrict__ o_,
+                                   int64_t n, long long ma, long long mb, int s, uint32_t *flags, int op_index) {
+  using TA = typename IntOf<AB>::T;
+  using TB = typename IntOf<BB>::T;
+  using TO = typename IntOf<OB>::T;
+  const TA *a = reinterpret_cast<const TA *>(a_);
+  const TB *b = reinterpret_cast<const TB *>(b_);
+  TO *o = reinterpret_cast<TO *>(o_);
+  int lo, hi;
+  dt_range(OB, lo, hi);
+  bool bad = false;
+  const long long rnd = round_term(s);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  constexpr int V = 8;                        // 8 elements per step: 8 B (i8) or 16 B (i16) per operand
+  const int64_t nv = n / V;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += stride) {
+    TA av[V];
+    TB bv[V];
+    TO ov[V];
+    if (AB == 1) *reinterpret_cast<uint2 *>(av) = reinterpret_cast<const uint2 *>(a)[v];
+    else *reinterpret_cast<uint4 *>(av) = reinterpret_cast<const uint4 *>(a)[v];
+    if (BB == 1) *reinterpret_cast<uint2 *>(bv) = reinterpret_cast<const uint2 *>(b)[v];
+    else *reinterpret_cast<uint4 *>(bv) = reinterpret_cast<const uint4 *>(b)[v];
+#pragma unroll
+    for (int q = 0; q < V; ++q) {
+      long long pa = (long long)av[q] * ma, pb = (long long)bv[q] * mb;
+      long long acc = pa + pb, r = acc + rnd;
+      if (CHECK) bad |= !fits_i32(pa) | !fits_i32(pb) | !fits_i32(acc) | !fits_i32(r);
+      ov[q] = (TO)clampi(r >> s, lo, hi);
+    }
+    if (OB == 1) reinterpret_cast<uint2 *>(o)[v] = *reinterpret_cast<uint2 *>(ov);
+    else reinterpret_cast<uint4 *>(o)[v] = *reinterpret_cast<uint4 *>(ov);
+  }
+  for (int64_t i = nv * V + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    long long pa = (long long)a[i] * ma, pb = (long long)b[i] * mb;
+    long long acc = pa + pb, r = acc + rnd;
+    if (CHECK) bad |= !fits_i32(pa) | !fits_i32(pb) | !fits_i32(acc) | !fits_i32(r);
+    o[i] = (TO)clampi(r >> s, lo, hi);
+  }
+  if (CHECK && __any_sync(0xffffffffu, bad) && bad) raise_flag(flags, FLAG_OVERFLOW, op_index);
+}
+
+// -------------------------------------------------------------------------------------------------- norms
+// rmsnorm_int / rmsnorm_wide (anvil/semantics.py:164-182) and the layernorm_int extension, one warp per row:
+//   [CENTER] mean = floor((sum x + d/2) / d), xc = x - mean       (else xc = x)
+//   ss = e + sum((xc^2 + 2^(c-1)) >> c);  idx, k = rsqrt_index(ss, n)  (while idx >= n: idx >>= 2, k++)
+//   out = clamp_i8(((xc*w*lut[idx])*M + 2^(s+k-1)) >> (s+k) [+ bias])
+template <int XB, bool CHECK>
+__global__ void norm_kernel(const void *__restrict__ x_, const int8_t *__restrict__ w,
+                            const int32_t *__restrict__ lut, const int8_t *__restrict__ bias,
+                            int8_t *__restrict__ out, int64_t rows, int d, int n, long long m, int s, int c,
+                            long long e, int center, uint32_t *flags, int op_index) {
+  using TX = typename IntOf<XB>::T;
+  const TX *x = reinterpret_cast<const TX *>(x_);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  bool bad = false, badidx = false;
+  const long long rc = round_term(c);
+  for (int64_t row = warp; row < rows; row += nwarps) {
+    const TX *xr = x + row * d;
+    long long mean = 0;
+    if (center) {
+      long long sum = 0;
+      for (int j = lane; j < d; j += 32) sum += xr[j];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (CHECK) bad |= !fits_i32(sum);
+      long long num = sum + d / 2;                        // floor division by d > 0
+      mean = num >= 0 ? num / d : -((-num + d - 1) / d);
+    }
+    long long ss = 0;
+    for (int j = lane; j < d; j += 32) {
+      long long xc = (long long)xr[j] - mean;
+      long long sq = xc * xc, sr = sq + rc;
+      if (CHECK) bad |= !fits_i32(sq) | !fits_i32(sr);
+      ss += sr >> c;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    ss += e;
+    if (CHECK) bad |= !fits_i32(ss);
+    long long idx = ss;
+    int k = 0;
+    while (idx >= n) { idx >>= 2; ++k; }
+    if (idx < 0) { badidx = true; idx = 0; }
+    const long long r = lut[idx];
+    const int sh = s + k;
+    if (sh > 31) bad = true;
+    const int shc = sh > 62 ? 62 : sh;
+    const long long rnd = round_term(shc > 31 ? 31 : shc);
+    int8_t *orow = out + row * d;
+    for (int j = lane; j < d; j += 32) {
+      long long xc = (long long)xr[j] - mean;
+      long long xw = xc * (long long)w[j];
+      long long xwr = xw * r;
+      long long p = xwr * m, q = p + rnd;
+      if (CHECK) bad |= !fits_i32(xw) | !fits_i32(xwr) | !fits_i32(p) | !fits_i32(q);
+      long long v = q >> shc;
+      if (bias) {
+        v += bias[j];
+      }
+      orow[j] = (int8_t)clampi(v, -128, 127);
+    }
+  }
+  if (CHECK && __any_sync(0xffffffffu, bad) && bad) raise_flag(flags, FLAG_OVERFLOW, op_index);
+  if (__any_sync(0xffffffffu, badidx) && badidx) raise_flag(flags, FLAG_INDEX, op_index);
+}
+
+// ------------------------------------------------------------------------------------------------ softmax
+// softmax_lut (anvil/lower/graph_to_tensor.py:352-398): one warp per row of (batch, T1, T2); kept j <= i when
+// causal; m = max(-128, x_j); e_j = lut[x_j - m + 255]; S = sum e_j; p_j = (e_j*one + S/2) / S (floor).
+template <int OB, bool CHECK>
+__global__ void softmax_kernel(const int8_t *__restrict__ x, const int32_t *__restrict__ lut_g, void *__restrict__ o_,
+                               int64_t rows, int t1, int t2, long long one, int causal, uint32_t *flags,
+                               int op_index) {
+  using TO = typename IntOf<OB>::T;
+  TO *o = reinterpret_cast<TO *>(o_);
+  __shared__ int32_t lut[256];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = lut_g[i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  bool bad = false;
+  for (int64_t row = warp; row < rows; row += nwarps) {
+    const int i = (int)(row % t1);
+    const int kept = causal ? (i + 1 < t2 ? i + 1 : t2) : t2;
+    const int8_t *xr = x + row * t2;
+    TO *orow = o + row * t2;
+    int mx = -128;
+    for (int j = lane; j < kept; j += 32) mx = max(mx, (int)xr[j]);
+#pragma unroll
+    for (int off = 16; off; off >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    long long tot = 0;
+    for (int j = lane; j < kept; j += 32) tot += lut[xr[j] - mx + 255];
+#pragma unroll
+    for (int off = 16; off; off >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, off);
+    if (CHECK) bad |= !fits_i32(tot) | (tot <= 0);
+    const long long half = tot / 2;
+    const long long den = tot > 0 ? tot : 1;
+    for (int j = lane; j < t2; j += 32) {
+      long long p = 0;
+      if (j < kept) {
+        long long eo = (long long)lut[xr[j] - mx + 255] * one;
+        long long num = eo + half;
+        if (CHECK) bad |= !fits_i32(eo) | !fits_i32(num) | (num < 0);
+        p = num >= 0 ? num / den : -((-num + den - 1) / den);
+      }
+      orow[j] = (TO)p;
+    }
+  }
+  if (CHECK && __any_sync(0xffffffffu, bad) && bad) raise_flag(flags, FLAG_OVERFLOW, op_index);
+}
+
+// ---------------------------------------------------------------------------------------------- transpose
+// Generic strided gather: out[i0..i5] = x[sum i_d * stride_d], rank <= 6 (anvil/interp/graph.py:76-78).
+struct TransposeDims {
+  int64_t n[6];
+  int64_t st[6];
+  int rank;
+};
+
+template <int EB>
+__global__ void transpose_kernel(const void *__restrict__ x_, void *__restrict__ o_, TransposeDims td, int64_t total) {
+  using T = typename IntOf<EB>::T;
+  const T *x = reinterpret_cast<const T *>(x_);
+  T *o = reinterpret_cast<T *>(o_);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+    int64_t rem = i, src = 0;
+    for (int dd = td.rank - 1; dd >= 0; --dd) {
+      int64_t q = rem / td.n[dd];
+      src += (rem - q * td.n[dd]) * td.st[dd];
+      rem = q;
+    }
+    o[i] = x[src];
+  }
+}
+
+// ------------------------------------------------------------------------------------------------- embed
+// x[b, t] = residual_add(wte[ids[b, t]], wpe[t], Ma, Mb, s), one warp per token (extension a11).
+template <bool CHECK>
+__global__ void embed_kernel(const int32_t *__restrict__ ids, const int8_t *__restrict__ wte,
+                             const int8_t *__restrict__ wpe, int8_t *__restrict__ out, int64_t rows, int t, int d,
+                             int64_t vocab, long long ma, long long mb, int s, uint32_t *flags, int op_index) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const long long rnd = round_term(s);
+  bool bad = false, badidx = false;
+  for (int64_t row = warp; row < rows; row += nwarps) {
+    const int64_t id = ids[row];
+    const int pos = (int)(row % t);
+    int8_t *orow = out + row * d;
+    if (id < 0 || id >= vocab) {
+      badidx = true;
+      for (int j = lane; j < d; j += 32) orow[j] = 0;
+      continue;
+    }
+    const int8_t *a = wte + id * d;
+    const int8_t *b = wpe + (int64_t)pos * d;
+    for (int j = lane; j < d; j += 32) {
+      long long pa = (long long)a[j] * ma, pb = (long long)b[j] * mb;
+      long long acc = pa + pb, r = acc + rnd;
+      if (CHECK) bad |= !fits_i32(pa) | !fits_i32(pb) | !fits_i32(acc) | !fits_i32(r);
+      orow[j] = (int8_t)clampi(r >> s, -128, 127);
+    }
+  }
+  if (CHECK && __any_sync(0xffffffffu, bad) && bad) raise_flag(flags, FLAG_OVERFLOW, op_index);
+  if (__any_sync(0xffffffffu, badidx) && badidx) raise_flag(flags, FLAG_INDEX, op_index);
+}
+
+}  // namespace anvil

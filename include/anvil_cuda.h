@@ -1,0 +1,159 @@
+/* libanvil_cuda.so: the C-ABI of Anvil's B200 (sm_100a) execution target.
+ *
+ * The reference runs a compiled graph through one backend call, anvil/runtime/api.py:127-141
+ * (run(job, backend) -> RunResult, ValueError on an unknown backend, TimeoutError on a hung launch), reached from
+ * CompiledModel.run (anvil/driver.py:305-322). The `cuda` target replaces the tiny-gpu Job/word-image pair with
+ * this library: the host (Python, over ctypes) lowers the graph to a list of anvil_op records with byte offsets
+ * into two device regions, and the library owns the device memory, launches the kernels on one stream per model
+ * and copies inputs/outputs. No torch types cross this boundary: plain pointers, sizes and POD structs.
+ *
+ * Every call returns ANVIL_OK (0) or a negative ANVIL_E_* code; anvil_last_error() gives the message of the
+ * last failure on the calling thread. A model handle is not re-entrant: one host thread at a time.
+ */
+#ifndef ANVIL_CUDA_H
+#define ANVIL_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define ANVIL_API __attribute__((visibility("default")))
+#else
+#define ANVIL_API
+#endif
+
+#define ANVIL_ABI_VERSION 1
+
+/* status codes (mapped to the reference's exception types by anvil/runtime/cuda.py) */
+#define ANVIL_OK 0
+#define ANVIL_E_BAD_ARG -1        /* ValueError    (anvil/runtime/api.py:104-124 validation)          */
+#define ANVIL_E_OOM -2            /* MemoryError   (anvil/memplan.py:27-28 MemoryPlanError analogue)  */
+#define ANVIL_E_CUDA -3           /* RuntimeError  (a CUDA API call failed)                            */
+#define ANVIL_E_TIMEOUT -4        /* TimeoutError  (a bounded device wait gave up, api.py:127-130)     */
+#define ANVIL_E_OVERFLOW -5       /* OverflowError (a checked int32 intermediate left int32,
+                                     anvil/semantics.py:47-49)                                        */
+#define ANVIL_E_INDEX -6          /* IndexError    (a LUT / token index outside its table,
+                                     anvil/semantics.py:76-84)                                        */
+#define ANVIL_E_UNSUPPORTED -7    /* NotImplementedError (no sm_100 device, op kind unknown)          */
+
+/* device buffer locations inside anvil_op.off[]: bit 63 set = the read-only const region, else the arena */
+#define ANVIL_LOC_CONST (1ull << 63)
+#define ANVIL_LOC_NONE (~0ull)
+
+/* op kinds: one per device kernel family (the graph ops of anvil/ir/graph.py:1-25 after lowering) */
+enum anvil_op_kind {
+  ANVIL_OP_GEMM = 1,        /* qmatmul / qlinear: requant(A @ B + bias, M, s) [-> lut]          (a1, a2, a10) */
+  ANVIL_OP_LUT = 2,         /* table[x + 128]                                                     (a3)      */
+  ANVIL_OP_LUT_MUL = 3,     /* requant(table[x + 128] * y, M, s)                                  (a4)      */
+  ANVIL_OP_ADD_REQUANT = 4, /* clamp((a*Ma + b*Mb + 2^(s-1)) >> s)                                (a7)      */
+  ANVIL_OP_NORM = 5,        /* rmsnorm_int / layernorm_int over the last axis                     (a5, a5x) */
+  ANVIL_OP_SOFTMAX = 6,     /* softmax_lut over the last axis                                     (a6)      */
+  ANVIL_OP_TRANSPOSE = 7,   /* strided copy (materialises a transpose)                           (a8)      */
+  ANVIL_OP_EMBED = 8,       /* add_requant(wte[ids], wpe[pos])                                    (a11)     */
+  ANVIL_OP_ATTENTION = 9,   /* fused causal qk^T -> softmax_lut -> p@v, scores kept on chip      (a1, a6)  */
+  ANVIL_OP_COPY = 10        /* contiguous byte copy (graph outputs that alias another buffer)              */
+};
+
+/* op flags */
+#define ANVIL_F_CAUSAL 1u     /* softmax / attention: row i keeps j <= i                          */
+#define ANVIL_F_CHECKED 2u    /* check every int32 intermediate on the device (sets the overflow flag) */
+#define ANVIL_F_LUT 4u        /* gemm: fused lut[. + 128] epilogue                                 */
+#define ANVIL_F_BIAS 8u       /* gemm: int32 bias per column; norm: int8 bias per channel          */
+#define ANVIL_F_CENTER 16u    /* norm: layernorm (mean-centre the row first)                        */
+#define ANVIL_F_SIMT 32u      /* gemm: force the CUDA-core kernel (shapes the TMA path cannot take) */
+
+/* One lowered kernel launch. Field meaning per kind (all sizes in elements, offsets in bytes):
+ *   GEMM        dims  = {batch, M, N, K}; strides = {a_batch, bt_batch (0: shared weight), out_batch,
+ *                       out_row}; off = {A (batch, M, K) int8, BT (batch|1, N, K) int8, OUT, LUT (256 i8),
+ *                       BIAS (N i32)}; mult = M, shift = s; out_bytes = 1 (i8) or 2 (i16)
+ *   LUT         dims  = {n}; off = {X, TABLE, OUT}
+ *   LUT_MUL     dims  = {n}; off = {X, Y, TABLE, OUT}; mult, shift
+ *   ADD_REQUANT dims  = {n}; off = {A, B, OUT}; in_bytes = a bytes, in2_bytes = b bytes, out_bytes;
+ *               ma, mb, shift
+ *   NORM        dims  = {rows, d, lut_len}; off = {X, W, LUT, OUT, BIAS}; in_bytes; mult, shift,
+ *               ss_shift, ss_init; flags CENTER / BIAS
+ *   SOFTMAX     dims  = {batch, T1, T2}; off = {X, LUT (256 i32), OUT}; one; out_bytes 1 or 4; flags CAUSAL
+ *   TRANSPOSE   dims  = {rank, n0, n1, n2, n3, n4, n5} (output dims); strides = input element strides per
+ *               output dim; off = {X, OUT}; in_bytes = element bytes
+ *   EMBED       dims  = {batch, T, d, vocab}; off = {IDS (i32), WTE, WPE, OUT}; ma, mb, shift
+ *   ATTENTION   dims  = {batch, heads, T, hd}; strides = {q_row, k_row, v_row, o_row} (row = token stride,
+ *               head h at column h*hd); off = {Q, K, V, OUT, EXP_LUT}; mult/shift = scores (M, s);
+ *               ma/mb = p@v (M, s) packed as mult2 = ma, shift2 = mb; one; flags CAUSAL
+ *   COPY        dims  = {bytes}; off = {X, OUT}
+ */
+typedef struct anvil_op {
+  int32_t kind;
+  uint32_t flags;
+  int32_t in_bytes;
+  int32_t in2_bytes;
+  int32_t out_bytes;
+  int32_t op_index;        /* graph op index, for error messages */
+  int64_t dims[8];
+  int64_t strides[8];
+  uint64_t off[8];
+  int64_t mult, shift, ma, mb, one, ss_shift, ss_init, mult2, shift2;
+} anvil_op;
+
+/* A host buffer bound to an arena range for one run (graph inputs and outputs). */
+typedef struct anvil_io {
+  uint64_t offset;         /* arena byte offset */
+  void *host;              /* host pointer (pinned or pageable) */
+  uint64_t bytes;
+} anvil_io;
+
+typedef struct anvil_model anvil_model;
+
+/* Library version and the message of the last failure on this thread (never NULL). */
+ANVIL_API int anvil_abi_version(void);
+ANVIL_API const char *anvil_last_error(void);
+
+/* Number of visible CUDA devices (0 without a driver); ANVIL_E_UNSUPPORTED if `device` is not sm_100. */
+ANVIL_API int anvil_device_count(int *count);
+ANVIL_API int anvil_cuda_init(int device);
+
+/* Create a model on `device`: uploads `const_bytes` of constants (weights, LUTs, biases, in device layout).
+ * Replaces the tiny-gpu image build of anvil/codegen/__init__.py:214 (program_job) for the cuda target. */
+ANVIL_API int anvil_model_create(int device, const void *consts, uint64_t const_bytes, anvil_model **out);
+
+/* Install the launch list for one batch size: validates every op against the region sizes, grows the device
+ * arena to `arena_bytes` (the liveness plan of anvil/memplan.py:190-198, in bytes) and builds the tensor maps. */
+ANVIL_API int anvil_model_prepare(anvil_model *m, const anvil_op *ops, int n_ops, uint64_t arena_bytes);
+
+/* One run: H2D copies of `inputs`, every op in order on the model's stream, D2H copies of `outputs`, then a
+ * stream synchronise. kernel_us (optional, n_ops floats) receives per-op device microseconds measured with CUDA
+ * events (adds one event pair per op). Overflow/index flags raised by checked kernels map to
+ * ANVIL_E_OVERFLOW / ANVIL_E_INDEX with the op index in the message. */
+ANVIL_API int anvil_model_run(anvil_model *m, const anvil_io *inputs, int n_inputs, const anvil_io *outputs, int n_outputs,
+                    float *kernel_us);
+
+/* The same launch chain on device-resident data (no host copies): `iters` back-to-back runs of every op,
+ * optionally captured once in a CUDA graph and replayed. Returns the device milliseconds of the whole loop
+ * (CUDA events on the model's stream) in *ms. Used by benchmarks to time kernels with inputs already in HBM. */
+ANVIL_API int anvil_model_run_device(anvil_model *m, int iters, int use_graph, float *ms);
+
+/* Read/write raw arena bytes (tests and keep="all" readback). */
+ANVIL_API int anvil_model_read(anvil_model *m, uint64_t offset, void *host, uint64_t bytes);
+ANVIL_API int anvil_model_write(anvil_model *m, uint64_t offset, const void *host, uint64_t bytes);
+
+/* Device pointer of the arena and of the const region (for callers that bring their own device buffers). */
+ANVIL_API int anvil_model_arena(anvil_model *m, uint64_t *arena_ptr, uint64_t *const_ptr);
+
+ANVIL_API void anvil_model_free(anvil_model *m);
+
+/* Standalone GEMM + requantize on caller-owned device memory (config 4 sweep; a1/a2 without a graph):
+ * out[M, N] = clamp((A[M, K] @ B[K, N] * mult + 2^(shift-1)) >> shift) as int8, with BT = B transposed
+ * ([N, K] row-major, K contiguous). Runs on `stream` (cudaStream_t, NULL = legacy default). `flags` takes
+ * ANVIL_F_CHECKED / ANVIL_F_SIMT. Bit-exact to requant(matmul_i8(A, B), mult, shift) (anvil/semantics.py:95-103)
+ * whenever that raises nothing. */
+ANVIL_API int anvil_gemm_requant(const int8_t *A, const int8_t *BT, int8_t *out, int64_t M, int64_t N, int64_t K,
+                       int32_t mult, int32_t shift, uint32_t flags, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ANVIL_CUDA_H */

@@ -1,0 +1,160 @@
+"""cuda target vs the CPU oracle, bit-exact, on a B200 (marked gpu).
+
+Every test calls through libanvil_cuda.so (the C-ABI): whole graphs via anvil.compile(...).run(x, "cuda"), the
+standalone GEMM via anvil_gemm_requant. Inputs are seeded; the oracle (oracle.interp / oracle.semantics) is the
+checker. Tolerance: none (integer outputs must be identical).
+"""
+import gzip
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import anvil
+from anvil.ir import parse_ir
+from anvil.runtime import cuda as C
+from oracle import interp
+from oracle import semantics as sem
+from graphs import random_case
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).parent / "golden"
+
+
+def _torch():
+    import torch
+    assert torch.cuda.is_available(), "a gpu test needs a CUDA device"
+    return torch
+
+
+def _check(got: dict, want: dict, syms=None):
+    syms = syms if syms is not None else want.keys()
+    for s in syms:
+        assert s in got, f"{s} not read back"
+        g, w = np.asarray(got[s]), np.asarray(want[s])
+        assert g.shape == w.shape, (s, g.shape, w.shape)
+        if not np.array_equal(g, w):
+            bad = np.argwhere(g != w)
+            raise AssertionError(f"{s}: {len(bad)} of {g.size} differ, first at {bad[0].tolist()}: "
+                                 f"{g[tuple(bad[0])]} != {w[tuple(bad[0])]}")
+
+
+# ------------------------------------------------------------------------------------------ standalone GEMM
+
+@pytest.mark.parametrize("m,n,k", [(1, 1, 16), (128, 64, 128), (130, 70, 48), (256, 256, 256), (1000, 300, 768),
+                                   (384, 512, 1024), (77, 33, 19)])
+@pytest.mark.parametrize("path", ["tc", "simt"])
+def test_gemm_requant_bit_exact(m, n, k, path):
+    torch = _torch()
+    rng = np.random.default_rng(m * 7 + n * 3 + k)
+    a = rng.integers(-127, 128, (m, k))
+    b = rng.integers(-127, 128, (k, n))
+    from anvil.frontend.numerics import fixed_point
+    (mult,), s = fixed_point([float(rng.uniform(2 ** -12, 2 ** -6))], [k * 127 * 127])
+    want = sem.requant(sem.matmul_i8(a, b), mult, s)
+    ta = torch.tensor(a, dtype=torch.int8, device="cuda")
+    tbt = torch.tensor(b.T.copy(), dtype=torch.int8, device="cuda")
+    out = torch.empty((m, n), dtype=torch.int8, device="cuda")
+    flags = C.F_CHECKED | (C.F_SIMT if path == "simt" else 0)
+    torch.cuda.synchronize()
+    C.gemm_requant(ta.data_ptr(), tbt.data_ptr(), out.data_ptr(), m, n, k, mult, s, flags,
+                   torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().astype(np.int64), want)
+
+
+# --------------------------------------------------------------------------------------------- whole graphs
+
+@pytest.mark.parametrize("seed", range(24))
+def test_random_graphs_small(seed):
+    m, c, x, want = random_case(seed, batch=3)
+    cm = anvil.compile(m, consts=c, prove=False)
+    got = cm.run([x[s] for s in cm.inputs], "cuda", quantized=True, keep="all").ints
+    _check(got, want.values)
+
+
+@pytest.mark.parametrize("seed", range(8))
+def test_random_graphs_tcgen05(seed):
+    m, c, x, want = random_case(1000 + seed, big=True, batch=2)
+    cm = anvil.compile(m, consts=c, prove=False, params=anvil.driver.CudaParams(gemm="tc"))
+    res = cm.run([x[s] for s in cm.inputs], "cuda", quantized=True)
+    _check(res.ints, want.values, cm.outputs)
+    res = cm.run([x[s] for s in cm.inputs], "cuda", quantized=True, keep="all")
+    _check(res.ints, want.values)
+
+
+def _frozen(name="frozen_model.json.gz"):
+    with gzip.open(GOLDEN / name, "rt") as f:
+        body = json.load(f)
+    module = parse_ir(body["ir"])
+    consts = {k: np.asarray(v, dtype=np.int64).reshape(body["shapes"][k]) for k, v in body["consts"].items()}
+    return module, consts, body
+
+
+def test_reference_frozen_model_all_75_values():
+    """The reference's own 2-layer RMSNorm/SwiGLU model (i16 residual), every value vs the fixture computed by the
+    reference's semantics module."""
+    module, consts, body = _frozen()
+    cm = anvil.compile(module, consts=consts)
+    x = np.asarray(body["x"])
+    res = cm.run(x, "cuda", quantized=True, keep="all")
+    want = {k: np.asarray(v) for k, v in body["values"].items()}
+    assert len(want) == 75
+    _check(res.ints, want)
+
+
+def test_reference_frozen_model_batched_and_fused():
+    module, consts, body = _frozen()
+    rng = np.random.default_rng(5)
+    xs = rng.integers(-(1 << 15), 1 << 15, (64,) + np.shape(body["x"]))
+    want = interp.run(module, {"x": xs}, consts, batch=True)
+    for gemm in ("auto", "tc", "simt"):
+        cm = anvil.compile(module, consts=consts, params=anvil.driver.CudaParams(gemm=gemm))
+        res = cm.run(xs, "cuda", quantized=True)
+        _check(res.ints, want.values, cm.outputs)
+
+
+def test_reference_i8_frozen_model():
+    module, consts, _ = _frozen("frozen_model_i8.json.gz")
+    rng = np.random.default_rng(6)
+    xs = rng.integers(-128, 128, (32, 16, 32))
+    want = interp.run(module, {"x": xs}, consts, batch=True)
+    cm = anvil.compile(module, consts=consts)
+    _check(cm.run(xs, "cuda", quantized=True, keep="all").ints, want.values)
+
+
+# ---------------------------------------------------------------------------------------- error behaviour
+
+def test_checked_overflow_raises_like_the_oracle():
+    from anvil.ir import GraphBuilder
+    g = GraphBuilder("ovf")
+    x = g.input("x", [4, 32])
+    w = g.const("w", [32, 8])
+    g.output(g.qlinear("y", x, w, 1 << 20, 4))
+    m = g.module()
+    c = {"w": np.full((32, 8), 127)}
+    xs = np.full((4, 32), 127)
+    with pytest.raises(OverflowError):
+        interp.run(m, {"x": xs}, c)
+    cm = anvil.compile(m, consts=c, prove=False)
+    assert cm.checked
+    with pytest.raises(OverflowError):
+        cm.run(xs, "cuda", quantized=True)
+    ok = cm.run(np.zeros((4, 32), dtype=np.int64), "cuda", quantized=True)       # the context is still usable
+    assert not ok.ints["y"].any()
+
+
+def test_embed_index_error():
+    from anvil.ir import GraphBuilder
+    g = GraphBuilder("emb")
+    ids = g.input("ids", [6], "i32")
+    g.output(g.embed("x", ids, g.const("wte", [10, 16]), g.const("wpe", [6, 16]), 1000, 1000, 11))
+    m = g.module()
+    rng = np.random.default_rng(1)
+    c = {"wte": rng.integers(-128, 128, (10, 16)), "wpe": rng.integers(-128, 128, (6, 16))}
+    cm = anvil.compile(m, consts=c)
+    ok = np.array([0, 3, 9, 2, 2, 1])
+    _check(cm.run(ok, "cuda", quantized=True).ints, interp.run(m, {"ids": ok}, c).values)
+    with pytest.raises(IndexError):
+        cm.run(np.array([0, 3, 10, 2, 2, 1]), "cuda", quantized=True)
