@@ -15,4 +15,11 @@ def compile(*args, **kw):  # noqa: A001  (the public entry point shadows the bui
     return _compile(*args, **kw)
 
 
-__all__ = ["compile"]
+def __getattr__(name):
+    if name in ("CudaParams", "CompiledModel", "RunOutput"):
+        from . import driver
+        return getattr(driver, name)
+    raise AttributeError(name)
+
+
+__all__ = ["compile", "CudaParams", "CompiledModel", "RunOutput"]

@@ -12,6 +12,7 @@ import numpy as np
 import pytest
 
 import anvil
+from anvil.driver import CudaParams
 from anvil.ir import parse_ir
 from anvil.runtime import cuda as C
 from oracle import interp
@@ -28,8 +29,8 @@ def _torch():
     return torch
 
 
-def _check(got: dict, want: dict, syms=None):
-    syms = syms if syms is not None else want.keys()
+def _check(got: dict, want: dict, syms=None, consts=()):
+    syms = syms if syms is not None else [k for k in want if k not in consts]
     for s in syms:
         assert s in got, f"{s} not read back"
         g, w = np.asarray(got[s]), np.asarray(want[s])
@@ -71,17 +72,17 @@ def test_random_graphs_small(seed):
     m, c, x, want = random_case(seed, batch=3)
     cm = anvil.compile(m, consts=c, prove=False)
     got = cm.run([x[s] for s in cm.inputs], "cuda", quantized=True, keep="all").ints
-    _check(got, want.values)
+    _check(got, want.values, consts=c)
 
 
 @pytest.mark.parametrize("seed", range(8))
 def test_random_graphs_tcgen05(seed):
     m, c, x, want = random_case(1000 + seed, big=True, batch=2)
-    cm = anvil.compile(m, consts=c, prove=False, params=anvil.driver.CudaParams(gemm="tc"))
+    cm = anvil.compile(m, consts=c, prove=False, params=CudaParams(gemm="tc"))
     res = cm.run([x[s] for s in cm.inputs], "cuda", quantized=True)
     _check(res.ints, want.values, cm.outputs)
     res = cm.run([x[s] for s in cm.inputs], "cuda", quantized=True, keep="all")
-    _check(res.ints, want.values)
+    _check(res.ints, want.values, consts=c)
 
 
 def _frozen(name="frozen_model.json.gz"):
@@ -101,7 +102,7 @@ def test_reference_frozen_model_all_75_values():
     res = cm.run(x, "cuda", quantized=True, keep="all")
     want = {k: np.asarray(v) for k, v in body["values"].items()}
     assert len(want) == 75
-    _check(res.ints, want)
+    _check(res.ints, want, consts=consts)
 
 
 def test_reference_frozen_model_batched_and_fused():
@@ -110,7 +111,7 @@ def test_reference_frozen_model_batched_and_fused():
     xs = rng.integers(-(1 << 15), 1 << 15, (64,) + np.shape(body["x"]))
     want = interp.run(module, {"x": xs}, consts, batch=True)
     for gemm in ("auto", "tc", "simt"):
-        cm = anvil.compile(module, consts=consts, params=anvil.driver.CudaParams(gemm=gemm))
+        cm = anvil.compile(module, consts=consts, params=CudaParams(gemm=gemm))
         res = cm.run(xs, "cuda", quantized=True)
         _check(res.ints, want.values, cm.outputs)
 
@@ -121,7 +122,7 @@ def test_reference_i8_frozen_model():
     xs = rng.integers(-128, 128, (32, 16, 32))
     want = interp.run(module, {"x": xs}, consts, batch=True)
     cm = anvil.compile(module, consts=consts)
-    _check(cm.run(xs, "cuda", quantized=True, keep="all").ints, want.values)
+    _check(cm.run(xs, "cuda", quantized=True, keep="all").ints, want.values, consts=consts)
 
 
 # ---------------------------------------------------------------------------------------- error behaviour
@@ -155,6 +156,6 @@ def test_embed_index_error():
     c = {"wte": rng.integers(-128, 128, (10, 16)), "wpe": rng.integers(-128, 128, (6, 16))}
     cm = anvil.compile(m, consts=c)
     ok = np.array([0, 3, 9, 2, 2, 1])
-    _check(cm.run(ok, "cuda", quantized=True).ints, interp.run(m, {"ids": ok}, c).values)
+    _check(cm.run(ok, "cuda", quantized=True).ints, interp.run(m, {"ids": ok}, c).values, consts=c)
     with pytest.raises(IndexError):
         cm.run(np.array([0, 3, 10, 2, 2, 1]), "cuda", quantized=True)
