@@ -52,14 +52,28 @@ class CudaParams:
             raise ValueError(f"CudaParams.gemm = {self.gemm!r}: auto, tc or simt")
 
 
-@dataclass
 class RunOutput:
-    output: np.ndarray                  # first graph output, dequantized (float)
-    outputs: list                       # every graph output, dequantized
-    ints: dict                          # sym -> int array of every value readable after the run
-    cycles: dict                        # launch label -> device microseconds (None unless run(..., timing=True))
-    result: object = None               # CudaRunResult
-    job: object = None                  # the DeviceProgram of device 0
+    """Result of CompiledModel.run (anvil/driver.py:56-76): `ints` holds every readable value as an integer array
+    in its graph dtype (int8 / int16 / int32); `output` / `outputs` are the dequantized graph outputs, computed
+    on first access."""
+
+    def __init__(self, model, ints: dict, cycles: dict, result=None, job=None):
+        self._model = model
+        self.ints = ints                # sym -> int array of every value readable after the run
+        self.cycles = cycles            # launch label -> device microseconds (None unless run(..., timing=True))
+        self.result = result            # CudaRunResult
+        self.job = job                  # the DeviceProgram of the first device
+        self._outs = None
+
+    @property
+    def outputs(self) -> list:
+        if self._outs is None:
+            self._outs = [self._model.dequantize(s, self.ints[s]) for s in self._model.outputs]
+        return self._outs
+
+    @property
+    def output(self) -> np.ndarray:
+        return self.outputs[0]
 
     @property
     def total_cycles(self):
@@ -268,12 +282,11 @@ class CompiledModel:
         if not batched:
             ints = {k: v[0] if v.ndim and v.shape[0] == 1 and k not in self._const_syms() else v
                     for k, v in ints.items()}
-        outs = [self.dequantize(s, ints[s]) for s in self.outputs]
         prog = self.program(shards[0][1], keep)
         cycles = {}
         for d, us in zip(prog.devops, kus if kus is not None else [None] * len(prog.devops)):
             cycles[d.label] = (cycles.get(d.label) or 0) + us if us is not None else None
-        return RunOutput(outs[0], outs, ints, cycles, CudaRunResult(batch, shards, cycles), prog)
+        return RunOutput(self, ints, cycles, CudaRunResult(batch, shards, cycles), prog)
 
     def _const_syms(self):
         return {op.sym_str for op in self.func.ops if isinstance(op, g.ConstOp)}
@@ -343,7 +356,7 @@ class CompiledModel:
         for sym, v in want.items():
             ints[sym] = _apply_view(roots[v.root], v)
         for sym in self.inputs:
-            ints.setdefault(sym, np.asarray(bound[sym], dtype=np.int64))
+            ints.setdefault(sym, bound[sym])
         return ints, kus
 
     def _readable(self, prog, keep):
@@ -382,11 +395,13 @@ class CompiledModel:
 
 
 def _apply_view(buf: np.ndarray, v) -> np.ndarray:
+    """The value of view `v` over its root buffer's bytes, as a fresh array of the view's dtype."""
     from .runtime.program import NP
     arr = buf.view(NP[v.dtype])
+    if v.contiguous:
+        return arr[: v.numel].reshape(v.shape)
     isz = arr.itemsize
-    out = np.lib.stride_tricks.as_strided(arr[v.offset:], v.shape, [s * isz for s in v.strides])
-    return np.array(out, dtype=np.int64)
+    return np.lib.stride_tricks.as_strided(arr[v.offset:], v.shape, [s * isz for s in v.strides]).copy()
 
 
 def compile(model, example_inputs=None, calib_inputs=None, params: CudaParams | None = None, schedules=None, *,

@@ -212,8 +212,12 @@ class Lowering:
 
     # ------------------------------------------------------------------------------------------- lowering
     def run(self):
+        for idx, op in enumerate(self.func.ops):          # consts first: a fused epilogue may need a later table
+            if isinstance(op, g.ConstOp):
+                self.idx = idx
+                self._ConstOp(op)
         for idx, op in enumerate(self.func.ops):
-            if idx in self.skip:
+            if idx in self.skip or isinstance(op, g.ConstOp):
                 continue
             self.idx = idx
             handler = getattr(self, "_" + type(op).__name__)

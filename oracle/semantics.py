@@ -108,11 +108,20 @@ def requant(acc, m, s):
     return requant_dtype(acc, m, s, "i8")
 
 
+EXACT_F64_K = 1 << 38          # K * 128 * 128 < 2^52: every partial sum of int8 products is exact in float64
+
+
 def matmul_i8(a, b):
-    """golden.matmul_i8: int8 operands, exact product summed in int64, the result checked int32. Batched as numpy
-    matmul broadcasts ((..., M, K) @ (K, N) or (..., M, K) @ (..., K, N))."""
+    """golden.matmul_i8: int8 operands, exact product summed, the result checked int32. Batched as numpy matmul
+    broadcasts ((..., M, K) @ (K, N) or (..., M, K) @ (..., K, N)). The sums are formed in float64 BLAS when K is
+    small enough that every partial sum of int8 products is an integer below 2^53 (always, in practice), which is
+    exact and equal to the int64 sum; otherwise in int64."""
     a, b = check_i8(a, "a"), check_i8(b, "b")
-    return check_i32(np.matmul(a, b), "a @ b")
+    if a.shape[-1] < EXACT_F64_K:
+        out = np.rint(np.matmul(a.astype(np.float64), b.astype(np.float64))).astype(np.int64)
+    else:
+        out = np.matmul(a, b)
+    return check_i32(out, "a @ b")
 
 
 def rsqrt_index(ss, n):
