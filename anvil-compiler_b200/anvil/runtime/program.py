@@ -15,7 +15,8 @@ B200 instead of a 4-thread toy core:
 * Fusions (only when keep="outputs", so every fused-away value is unobservable): a `lut` whose input is a GEMM
   result used nowhere else becomes the GEMM's LUT epilogue (bit-identical: qmatmul with lut =
   lut_i8(requant(.)), anvil/semantics.py:95-103); the head-batched qk^T -> softmax_lut -> p@v chain becomes one
-  fused attention launch when the shapes allow (anvil.runtime.fusion).
+  fused attention launch when the shapes allow (hd 64 or 128, T2 <= 1024), its V projection writing V^T
+  head-major so the P @ V MMA reads it K-major, and its output landing in the merged-heads layout.
 * Activation buffers are placed by anvil.memplan (liveness, 256-byte aligned offsets).
 """
 from __future__ import annotations
@@ -65,6 +66,53 @@ class View:
     def permute(self, perm) -> "View":
         return View(self.root, self.const, tuple(self.shape[p] for p in perm),
                     tuple(self.strides[p] for p in perm), self.offset, self.dtype)
+
+
+def view_reshape(v: "View", new_shape) -> "View | None":
+    """v reshaped to new_shape without moving data, or None when the strides do not allow it (numpy's no-copy
+    reshape rule: each group of old dims that maps onto a group of new dims must be contiguous within itself)."""
+    new_shape = tuple(int(d) for d in new_shape)
+    if math.prod(new_shape) != v.numel:
+        return None
+    old = [(d, s) for d, s in zip(v.shape, v.strides) if d != 1]
+    new = [d for d in new_shape if d != 1]
+    out, i, j = [], 0, 0
+    while i < len(old) or j < len(new):
+        if i >= len(old) or j >= len(new):
+            return None
+        gi, gj = [old[i]], [new[j]]
+        po, pn = old[i][0], new[j]
+        i += 1
+        j += 1
+        while po != pn:
+            if po < pn:
+                if i >= len(old):
+                    return None
+                gi.append(old[i])
+                po *= old[i][0]
+                i += 1
+            else:
+                if j >= len(new):
+                    return None
+                gj.append(new[j])
+                pn *= new[j]
+                j += 1
+        for (d0, s0), (d1, s1) in zip(gi, gi[1:]):
+            if s0 != s1 * d1:
+                return None
+        st = gi[-1][1]
+        strides = []
+        for d in reversed(gj):
+            strides.append(st)
+            st *= d
+        out.extend(reversed(strides))
+    it = iter(out)
+    full = []
+    for d in new_shape:
+        full.append(next(it) if d != 1 else 0)
+    full = tuple(full)
+    # size-1 dims: any stride; give them the next dim's extent for a tidy view
+    return View(v.root, v.const, new_shape, full, v.offset, v.dtype)
 
 
 @dataclass
@@ -212,6 +260,7 @@ class Lowering:
 
     # ------------------------------------------------------------------------------------------- lowering
     def run(self):
+        self.detect_fusions()
         for idx, op in enumerate(self.func.ops):          # consts first: a fused epilogue may need a later table
             if isinstance(op, g.ConstOp):
                 self.idx = idx
@@ -250,9 +299,12 @@ class Lowering:
                 x = View(key, True, x.shape, row_major(x.shape), 0, x.dtype)
             self.views[id(op.result)] = View(x.root, True, tuple(t.dims), row_major(t.dims), x.offset, x.dtype)
             return
-        x = self.contig(x, op.sym_str or "reshape")
         shape = (self.B,) + tuple(t.dims)
-        self.views[id(op.result)] = View(x.root, False, shape, row_major(shape), x.offset, x.dtype)
+        rv = view_reshape(x, shape)
+        if rv is None:
+            x = self.contig(x, op.sym_str or "reshape")
+            rv = View(x.root, False, shape, row_major(shape), x.offset, x.dtype)
+        self.views[id(op.result)] = rv
 
     def _TransposeOp(self, op):
         x = self.views[id(op.x)]
@@ -266,6 +318,10 @@ class Lowering:
 
     # ---- GEMM
     def _gemm(self, op):
+        if id(op) in self.attn:            # the scores matmul: emitted with the p@v matmul, once V exists
+            return
+        if id(op) in self.attn_o:
+            return self._attention(*self.attn_o[id(op)])
         a = self.views[id(op.a)]
         b = self.views[id(op.b)]
         t = g.qt(op.result)
@@ -317,6 +373,13 @@ class Lowering:
             outs_shape = a.shape[:-1] + (N,)
             per_sample = [(0, 0)]
         out = self.new_view(out_label, outs_shape, t.dtype)
+        ostrides = [Mt * N, N, 0, 0, 1]
+        if id(op) in self.vt_gemm and batch == 1 and len(per_sample) == 1 and lut_slot is None:
+            # head-major transposed output for a fused attention's V: element (b, t, c) at b*C*T + c*T + t
+            T = self.vt_gemm[id(op)]
+            ostrides = [Mt * N, 1, T, N * T, T]
+            out = View(out.root, False, out.shape, (N * T, 1, T), 0, out.dtype)
+            self.fused.append(f"{label}:vT_epilogue")
         if self.gemm_mode == "simt" or (self.gemm_mode == "auto" and Mt * N * K * batch < SIMT_MAX_WORK):
             flags |= C.F_SIMT
         for s_a, _ in per_sample:
@@ -325,7 +388,8 @@ class Lowering:
             slots = [self.act_slot(a, a_elem), bt_slot if bt_slot is not None else self.act_slot(bt),
                      self.act_slot(out, o_elem), lut_slot, bias_slot]
             self.emit(C.OP_GEMM, slots,
-                      {"dims": [batch, Mt, N, K], "strides": [a_bs, bt_bs, Mt * N, N], "mult": op.M, "shift": op.s,
+                      {"dims": [batch, Mt, N, K], "strides": [a_bs, bt_bs] + ostrides[:2] + ostrides[2:],
+                       "mult": op.M, "shift": op.s,
                        "out_bytes": ISZ[t.dtype], "flags": flags}, out_label, reads, [out.root],
                       {"ops": 2 * batch * Mt * N * K, "bytes": batch * Mt * K + N * K * (batch if bt_bs else 1)
                        + batch * Mt * N * ISZ[t.dtype]})
@@ -336,6 +400,84 @@ class Lowering:
 
     _QMatmulOp = _gemm
     _QLinearOp = _gemm
+
+    # ---- fused attention
+    def _attention(self, sop, pop, oop):
+        label = oop.sym_str or "attention"
+        q = self.views[id(sop.a)]                       # (B, H, T1, hd)
+        kT = self.views[id(sop.b)]                      # (B, H, hd, T2)
+        vh = self.views[id(oop.b)]                      # (B, H, T2, hd)
+        B, H, T1, hd = q.shape
+        T2 = kT.shape[-1]
+        k = kT.permute([0, 1, 3, 2])
+
+        def tma_ok(v):
+            return v.strides[-1] == 1 and all(st % 16 == 0 for st in v.strides[:-1]) and v.offset % 16 == 0
+
+        if not tma_ok(q):
+            q = self.contig(q, f"{label}.q")
+        if not tma_ok(k):
+            k = self.contig(k, f"{label}.k")
+        vt = vh.permute([0, 1, 3, 2])                   # (B, H, hd, T2), must be dense
+        if not vt.contiguous:
+            vt = self.contig(vt, f"{label}.vT")
+        out = self.new_view(label, (B, T1, H * hd), "i8")
+        flags = C.F_CAUSAL if pop.causal_bool else 0
+        kept = sum(min(i + 1, T2) for i in range(T1)) if pop.causal_bool else T1 * T2
+        self.emit(C.OP_ATTENTION,
+                  [self.act_slot(q), self.act_slot(k), self.act_slot(vt), self.act_slot(out),
+                   self._const(pop.lut, label, np.int32)],
+                  {"dims": [B, H, T1, T2, hd],
+                   "strides": [q.strides[0], q.strides[1], q.strides[2], k.strides[0], k.strides[1], k.strides[2],
+                               T1 * H * hd, H * hd],
+                   "mult": sop.M, "shift": sop.s, "mult2": oop.M, "shift2": oop.s, "one": pop.one, "flags": flags},
+                  label, [q.root, k.root, vt.root], [out.root], {"ops": 4 * hd * kept * B * H})
+        self.views[id(oop.result)] = View(out.root, False, (B, H, T1, hd), (T1 * H * hd, hd, H * hd, 1), 0, "i8")
+        self.fused.append(f"{sop.sym_str}+{pop.sym_str}+{label}:attention")
+
+    def detect_fusions(self):
+        """Find head-batched qk^T -> softmax_lut -> p@v chains the fused attention kernel can run, and the V
+        projections that can write V^T for them."""
+        self.attn, self.attn_o, self.vt_gemm = {}, {}, {}
+        if not self.fuse or self.checked:
+            return
+        uses = self.uses
+        single = lambda v, op: uses.get(id(v), []) == [op] and id(v) not in self.out_ids  # noqa: E731
+        for op in self.func.ops:
+            if not isinstance(op, g.SoftmaxLutOp) or g.qt(op.result).dtype != "i8" or op.one > 127:
+                continue
+            sop = op.x.owner
+            if not isinstance(sop, g.QMatmulOp) or sop.lut is not None or g.qt(sop.result).dtype != "i8":
+                continue
+            if not single(op.x, op):
+                continue
+            us = uses.get(id(op.result), [])
+            if len(us) != 1 or id(op.result) in self.out_ids:
+                continue
+            oop = us[0]
+            if not isinstance(oop, g.QMatmulOp) or oop.a is not op.result or oop.lut is not None or \
+                    g.qt(oop.result).dtype != "i8":
+                continue
+            qd, kd, vd = g.qt(sop.a).dims, g.qt(sop.b).dims, g.qt(oop.b).dims
+            if len(qd) != 3 or len(kd) != 3 or len(vd) != 3:
+                continue
+            H, T1, hd = qd
+            T2 = kd[-1]
+            if hd not in (64, 128) or T2 > 1024 or T2 % 16 or vd != (H, T2, hd) or kd != (H, hd, T2):
+                continue
+            self.attn[id(sop)] = (op, oop)
+            self.attn_o[id(oop)] = (sop, op, oop)
+            self.skip.add(self.func.ops.index(op))
+            # V^T straight from the V projection: vh = transpose(reshape(v, [T2, H, hd]), [1, 0, 2])
+            tr = oop.b.owner
+            if isinstance(tr, g.TransposeOp) and tr.perm_list == [1, 0, 2] and single(oop.b, oop):
+                rs = tr.x.owner
+                if isinstance(rs, g.ReshapeOp) and single(tr.x, tr) and g.qt(rs.result).dims == (T2, H, hd):
+                    vop = rs.x.owner
+                    if isinstance(vop, (g.QLinearOp, g.QMatmulOp)) and single(rs.x, rs) and vop.lut is None \
+                            and len(g.qt(vop.b).dims) == 2 and g.qt(vop.result).dims == (T2, H * hd) \
+                            and g.qt(vop.result).dtype == "i8":
+                        self.vt_gemm[id(vop)] = T2
 
     # ---- memory-bound ops
     def _act(self, value, label):
@@ -430,12 +572,6 @@ class Lowering:
 def lower_program(module, consts: dict, pool: ConstPool, batch: int, keep="outputs", checked=False, fuse=True,
                   gemm="auto") -> DeviceProgram:
     L = Lowering(module, consts, pool, batch, keep, checked, fuse, gemm)
-    try:
-        from . import fusion
-        if L.fuse:
-            fusion.apply(L)
-    except ImportError:
-        pass
     L.run()
     func = L.func
     outs = []

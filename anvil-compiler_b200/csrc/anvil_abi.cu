@@ -17,6 +17,7 @@
 
 #include "../../include/anvil_cuda.h"
 #include "common.cuh"
+#include "attention.cuh"
 #include "gemm.cuh"
 #include "rowops.cuh"
 
@@ -81,6 +82,27 @@ static int make_map_i8(CUtensorMap *map, const void *base, uint64_t x, uint64_t 
   return ANVIL_OK;
 }
 
+// General int8 tiled map: rank 2..4, dims/strides in elements = bytes, given box and swizzle.
+static int make_map(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides,
+                    const uint32_t *box, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return fail(ANVIL_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i) st[i - 1] = strides[i - 1];
+  }
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void *>(base), d, st, bx, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ANVIL_E_CUDA, "cuTensorMapEncodeTiled (rank %d) failed (%d)", rank, (int)r);
+  return ANVIL_OK;
+}
+
 // ------------------------------------------------------------------------------------------------- model
 
 struct Launch {
@@ -90,8 +112,10 @@ struct Launch {
   // GEMM tensor-core path
   bool tc = false;
   int bn = 0;
-  CUtensorMap mapA, mapB;
+  CUtensorMap mapA, mapB, mapC;
   GemmParams gp;
+  AttnParams ap;
+  int hd = 0;
 };
 
 struct anvil_model {
@@ -163,9 +187,11 @@ extern "C" int anvil_model_create(int device, const void *consts, uint64_t const
       return cleanup(fail(ANVIL_E_CUDA, "const upload failed"));
   }
   m->const_bytes = const_bytes;
-  static bool attrs = false;       // per process: the attribute is per function, valid on every device
-  if (!attrs) {
+  static bool attrs[64] = {};     // the attribute is per function and per device
+  if (device < 64 && !attrs[device]) {
     int r = 0;
+    r |= set_smem(attn_kernel<64>, AttnCfg<64>::SMEM_BYTES);
+    r |= set_smem(attn_kernel<128>, AttnCfg<128>::SMEM_BYTES);
     r |= set_smem(qgemm_tc_kernel<64, 1>, TcCfg<64>::SMEM_BYTES);
     r |= set_smem(qgemm_tc_kernel<64, 2>, TcCfg<64>::SMEM_BYTES);
     r |= set_smem(qgemm_tc_kernel<128, 1>, TcCfg<128>::SMEM_BYTES);
@@ -173,7 +199,7 @@ extern "C" int anvil_model_create(int device, const void *consts, uint64_t const
     r |= set_smem(qgemm_tc_kernel<256, 1>, TcCfg<256>::SMEM_BYTES);
     r |= set_smem(qgemm_tc_kernel<256, 2>, TcCfg<256>::SMEM_BYTES);
     if (r) return cleanup(ANVIL_E_CUDA);
-    attrs = true;
+    attrs[device] = true;
   }
   *out = m;
   return ANVIL_OK;
@@ -220,11 +246,17 @@ static int prepare_gemm(anvil_model *m, Launch &L) {
   if (batch < 1 || M < 1 || N < 1 || K < 1) return fail(ANVIL_E_BAD_ARG, "op %d: bad gemm dims", op.op_index);
   if (op.out_bytes != 1 && op.out_bytes != 2) return fail(ANVIL_E_BAD_ARG, "op %d: gemm output must be i8 or i16", op.op_index);
   if (op.shift < 0 || op.shift > 31) return fail(ANVIL_E_BAD_ARG, "op %d: shift %lld outside [0, 31]", op.op_index, (long long)op.shift);
-  if (a_bs < 0 || bt_bs < 0 || o_bs < 0 || o_rs < N) return fail(ANVIL_E_BAD_ARG, "op %d: bad gemm strides", op.op_index);
+  const int64_t o_grp = op.strides[4], o_gs = op.strides[5], o_cs = op.strides[6] ? op.strides[6] : 1;
+  if (a_bs < 0 || bt_bs < 0 || o_bs < 0 || o_rs < 0 || o_grp < 0 || o_gs < 0 || o_cs < 1 ||
+      (o_cs == 1 && o_rs < N))
+    return fail(ANVIL_E_BAD_ARG, "op %d: bad gemm strides", op.op_index);
   int rc;
   const uint64_t a_bytes = (uint64_t)((batch - 1) * a_bs + M * K);
   const uint64_t b_bytes = (uint64_t)((bt_bs ? (batch - 1) * bt_bs : 0) + N * K);
-  const uint64_t o_bytes = (uint64_t)(((batch - 1) * o_bs + (M - 1) * o_rs + N) * op.out_bytes);
+  const int64_t R = o_grp ? o_grp : M;
+  const int64_t last_row = M - 1;
+  const uint64_t o_bytes = (uint64_t)(((batch - 1) * o_bs + (last_row / R) * o_gs + std::min<int64_t>(R - 1, last_row) * o_rs +
+                                       (N - 1) * o_cs + 1) * op.out_bytes);
   if ((rc = resolve(m, op, 0, a_bytes, &L.ptr[0]))) return rc;
   if ((rc = resolve(m, op, 1, b_bytes, &L.ptr[1]))) return rc;
   if ((rc = resolve(m, op, 2, o_bytes, &L.ptr[2]))) return rc;
@@ -234,6 +266,9 @@ static int prepare_gemm(anvil_model *m, Launch &L) {
   memset(&p, 0, sizeof p);
   p.batch = batch; p.M = M; p.N = N; p.K = K;
   p.a_bstride = a_bs; p.bt_bstride = bt_bs; p.o_bstride = o_bs; p.o_rstride = o_rs;
+  p.o_group = op.strides[4];
+  p.o_gstride = op.strides[5];
+  p.o_cstride = op.strides[6] ? op.strides[6] : 1;
   p.A = (const int8_t *)L.ptr[0];
   p.BT = (const int8_t *)L.ptr[1];
   p.out = L.ptr[2];
@@ -258,6 +293,59 @@ static int prepare_gemm(anvil_model *m, Launch &L) {
   const uint64_t b_z = bt_bs ? batch : 1, b_zs = bt_bs ? bt_bs : N * K;
   if ((rc = make_map_i8(&L.mapA, p.A, K, M, a_z, K, a_zs, TC_BM))) return rc;
   if ((rc = make_map_i8(&L.mapB, p.BT, K, N, b_z, K, b_zs, L.bn))) return rc;
+  return ANVIL_OK;
+}
+
+// ATTENTION: dims = {B, H, T1, T2, hd}; strides = {q_b, q_h, q_t, k_b, k_h, k_t, o_b, o_t};
+// off = {Q, K, VT (dense (B, H, hd, T2)), OUT, EXP_LUT}
+static int prepare_attention(anvil_model *m, Launch &L) {
+  const anvil_op &op = L.op;
+  const int64_t B = op.dims[0], H = op.dims[1], T1 = op.dims[2], T2 = op.dims[3], HD = op.dims[4];
+  const int64_t *st = op.strides;
+  if (B < 1 || H < 1 || T1 < 1 || T2 < 1 || (HD != 64 && HD != 128))
+    return fail(ANVIL_E_BAD_ARG, "op %d: attention needs hd 64 or 128 (got %lld)", op.op_index, (long long)HD);
+  if (T2 > 1024 || T2 % 16) return fail(ANVIL_E_BAD_ARG, "op %d: attention needs T2 <= 1024, T2 % 16 == 0", op.op_index);
+  for (int i = 0; i < 8; ++i)
+    if (st[i] < 0 || st[i] % 16) return fail(ANVIL_E_BAD_ARG, "op %d: attention strides must be multiples of 16", op.op_index);
+  if (op.one < 1 || op.one > 127 || op.shift < 0 || op.shift > 31 || op.shift2 < 0 || op.shift2 > 31)
+    return fail(ANVIL_E_BAD_ARG, "op %d: bad attention constants", op.op_index);
+  int rc;
+  const uint64_t qb = (B - 1) * st[0] + (H - 1) * st[1] + (T1 - 1) * st[2] + HD;
+  const uint64_t kb = (B - 1) * st[3] + (H - 1) * st[4] + (T2 - 1) * st[5] + HD;
+  const uint64_t vb = B * H * HD * T2;
+  const uint64_t ob = (B - 1) * st[6] + (T1 - 1) * st[7] + H * HD;
+  if ((rc = resolve(m, op, 0, qb, &L.ptr[0]))) return rc;
+  if ((rc = resolve(m, op, 1, kb, &L.ptr[1]))) return rc;
+  if ((rc = resolve(m, op, 2, vb, &L.ptr[2]))) return rc;
+  if ((rc = resolve(m, op, 3, ob, &L.ptr[3]))) return rc;
+  if ((rc = resolve(m, op, 4, 1024, &L.ptr[4]))) return rc;
+  for (int i = 0; i < 3; ++i)
+    if (!aligned16(L.ptr[i])) return fail(ANVIL_E_BAD_ARG, "op %d: attention operand %d not 16-byte aligned", op.op_index, i);
+  const CUtensorMapSwizzle qk_swz = HD == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+  const uint64_t qdims[4] = {(uint64_t)HD, (uint64_t)H, (uint64_t)T1, (uint64_t)B};
+  const uint64_t qstr[3] = {(uint64_t)st[1], (uint64_t)st[2], (uint64_t)(B > 1 ? st[0] : st[2] * T1)};
+  const uint32_t qbox[4] = {(uint32_t)HD, 1, 128, 1};
+  if ((rc = make_map(&L.mapA, L.ptr[0], 4, qdims, qstr, qbox, qk_swz))) return rc;
+  const uint64_t kdims[4] = {(uint64_t)HD, (uint64_t)H, (uint64_t)T2, (uint64_t)B};
+  const uint64_t kstr[3] = {(uint64_t)st[4], (uint64_t)st[5], (uint64_t)(B > 1 ? st[3] : st[5] * T2)};
+  if ((rc = make_map(&L.mapB, L.ptr[1], 4, kdims, kstr, qbox, qk_swz))) return rc;
+  const uint64_t vdims[2] = {(uint64_t)T2, (uint64_t)(B * H * HD)};
+  const uint64_t vstr[1] = {(uint64_t)T2};
+  const uint32_t vbox[2] = {128, (uint32_t)HD};
+  if ((rc = make_map(&L.mapC, L.ptr[2], 2, vdims, vstr, vbox, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+  AttnParams &a = L.ap;
+  memset(&a, 0, sizeof a);
+  a.B = (int)B; a.H = (int)H; a.T1 = (int)T1; a.T2 = (int)T2;
+  a.nqt = (int)((T1 + 127) / 128);
+  a.o_bs = st[6]; a.o_rs = st[7];
+  a.out = (int8_t *)L.ptr[3];
+  a.lut = (const int32_t *)L.ptr[4];
+  a.m1 = op.mult; a.s1 = (int)op.shift; a.m2 = op.mult2; a.s2 = (int)op.shift2;
+  a.one = (int)op.one;
+  a.causal = (op.flags & ANVIL_F_CAUSAL) ? 1 : 0;
+  a.flags = m->flags;
+  a.op_index = op.op_index;
+  L.hd = (int)HD;
   return ANVIL_OK;
 }
 
@@ -318,6 +406,8 @@ static int prepare_op(anvil_model *m, Launch &L) {
     case ANVIL_OP_COPY:
       if ((rc = resolve(m, op, 0, d[0], &L.ptr[0]))) return rc;
       return resolve(m, op, 1, d[0], &L.ptr[1]);
+    case ANVIL_OP_ATTENTION:
+      return prepare_attention(m, L);
     default:
       return fail(ANVIL_E_UNSUPPORTED, "op %d: unknown kind %d", op.op_index, op.kind);
   }
@@ -456,6 +546,16 @@ static int launch_op(anvil_model *m, Launch &L) {
     case ANVIL_OP_COPY:
       CK(cudaMemcpyAsync(L.ptr[1], L.ptr[0], d[0], cudaMemcpyDeviceToDevice, st));
       break;
+    case ANVIL_OP_ATTENTION: {
+      const AttnParams &a = L.ap;
+      const int64_t grid = (int64_t)a.B * a.H * a.nqt;
+      if (grid > 0x7fffffff) return fail(ANVIL_E_BAD_ARG, "op %d: attention grid too large", oi);
+      if (L.hd == 64)
+        attn_kernel<64><<<(unsigned)grid, 192, AttnCfg<64>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, a);
+      else
+        attn_kernel<128><<<(unsigned)grid, 192, AttnCfg<128>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, a);
+      break;
+    }
     default:
       return fail(ANVIL_E_UNSUPPORTED, "op %d: unknown kind %d", oi, op.kind);
   }
@@ -617,6 +717,7 @@ extern "C" int anvil_gemm_requant(const int8_t *A, const int8_t *BT, int8_t *out
   memset(&p, 0, sizeof p);
   p.batch = 1; p.M = M; p.N = N; p.K = K;
   p.o_rstride = N;
+  p.o_cstride = 1;
   p.A = A; p.BT = BT; p.out = out;
   p.mult = mult; p.shift = shift; p.out_bytes = 1;
   p.check = (flags & ANVIL_F_CHECKED) ? 1 : 0;

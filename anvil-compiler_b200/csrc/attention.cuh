@@ -1,0 +1,316 @@
+// Fused causal attention with Anvil's integer softmax, scores kept on chip:
+//   scores = requant(q . k^T, M1, s1)                                  (qmatmul, anvil/semantics.py:95-103)
+//   p      = softmax_lut(scores, exp_lut, one, causal)                  (anvil/lower/graph_to_tensor.py:352-398)
+//   o      = requant(p @ v, M2, s2), written straight into the merged-heads layout (b, t, h*hd + d)
+//
+// One CTA per (batch, head, 128-query tile), heaviest causal tiles first. Warp roles:
+//   warp 0     TMA: the Q tile once, then K tiles (128 keys x hd) into a KS-deep ring, then V^T slabs
+//              (hd x 128 keys, from the head-major transposed V the v-projection GEMM writes) into a VS-deep ring
+//   warp 1     tcgen05.mma kind::i8: S_j = Q K_j^T into one of two TMEM buffers (128 x 128 int32); after the
+//              softmax, O = sum_j P_j V_j into a third TMEM region (128 x hd)
+//   warps 2-5  one thread per query row: drain S_j from TMEM, requant to int8, track the row max, store the row
+//              into the P slab j in shared memory (the 128-byte-swizzled K-major layout the P @ V MMA reads);
+//              then the two exact softmax passes over the slabs (sum of exp_lut, then (e*one + S/2) / S by a
+//              float reciprocal with an integer correction step), then O from TMEM -> requant -> global
+// The whole score row (up to 1024 keys, int8) stays in shared memory, so the row max and row sum are exact before
+// any probability is formed, as the reference's three-stage loop nest requires; an online (rescaled) softmax
+// would not be bit-exact.
+#pragma once
+
+#include "common.cuh"
+
+namespace anvil {
+
+struct AttnParams {
+  int B, H, T1, T2, nqt;
+  int64_t o_bs, o_rs;                  // out element (b, t, h*hd + d) = b*o_bs + t*o_rs + h*hd + d
+  int8_t *out;
+  const int32_t *lut;                  // 256 x i32 exp LUT
+  long long m1, m2;
+  int s1, s2, one, causal;
+  uint32_t *flags;
+  int op_index;
+};
+
+template <int HD>
+struct AttnCfg {
+  static constexpr int KS = HD == 64 ? 3 : 2;
+  static constexpr int VS = HD == 64 ? 3 : 2;
+  static constexpr int Q_BYTES = 128 * HD;
+  static constexpr int K_BYTES = 128 * HD;
+  static constexpr int V_BYTES = HD * 128;
+  static constexpr int MAX_SLABS = 8;                   // T2 <= 1024
+  static constexpr int P_SLAB = 128 * 128;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_V = OFF_K + KS * K_BYTES;
+  static constexpr int OFF_P = OFF_V + VS * V_BYTES;
+  static constexpr int OFF_LUT = OFF_P + MAX_SLABS * P_SLAB;
+  static constexpr int OFF_BAR = OFF_LUT + 1024;
+  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 1 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+  // Q / K tiles: rows of HD bytes. 64-byte rows use the 64-byte swizzle (8-row atoms of 512 B), 128-byte rows
+  // the 128-byte swizzle (1024 B atoms); the descriptor layout types are 4 and 2.
+  static constexpr uint32_t QK_LAYOUT = HD == 64 ? 4u : 2u;
+  static constexpr uint32_t QK_SBO = HD == 64 ? 512u : 1024u;
+};
+
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t smem_addr, uint32_t layout, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(sbo >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)layout << 61;
+  return d;
+}
+
+__device__ __forceinline__ void tma_load_4d(void *smem_dst, const CUtensorMap *map, int x, int y, int z, int w,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// byte offset of 16-byte chunk `ch` (0..7) of row `r` (0..127) inside one 128 x 128 P slab (SW128 K-major)
+__device__ __forceinline__ int pslab_off(int r, int ch) { return (r >> 3) * 1024 + (r & 7) * 128 + ((ch ^ (r & 7)) << 4); }
+
+template <int HD>
+__global__ void __launch_bounds__(192, 1)
+    attn_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
+                const __grid_constant__ CUtensorMap mapV, const AttnParams p) {
+  using Cfg = AttnCfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::OFF_BAR);
+  uint64_t *qfull = bars;
+  uint64_t *kfull = qfull + 1, *kempty = kfull + Cfg::KS;
+  uint64_t *vfull = kempty + Cfg::KS, *vempty = vfull + Cfg::VS;
+  uint64_t *sfull = vempty + Cfg::VS, *sempty = sfull + 2;
+  uint64_t *pready = sempty + 2, *ofull = pready + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Cfg::OFF_MISC);
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + Cfg::OFF_MISC + 4);
+  int32_t *lut = reinterpret_cast<int32_t *>(smem + Cfg::OFF_LUT);
+  uint8_t *pbuf = smem + Cfg::OFF_P;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int BH = p.B * p.H;
+  const int qt = p.nqt - 1 - (int)(blockIdx.x / BH);
+  const int bh = (int)(blockIdx.x % BH);
+  const int b = bh / p.H, h = bh % p.H;
+  const int q0 = qt * 128;
+  const int kv_end = p.causal ? min(p.T2, q0 + 128) : p.T2;
+  const int nkv = (kv_end + 127) / 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(qfull, 1);
+    for (int i = 0; i < Cfg::KS; ++i) { mbar_init(&kfull[i], 1); mbar_init(&kempty[i], 1); }
+    for (int i = 0; i < Cfg::VS; ++i) { mbar_init(&vfull[i], 1); mbar_init(&vempty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&sfull[i], 1); mbar_init(&sempty[i], 128); }
+    mbar_init(pready, 128);
+    mbar_init(ofull, 1);
+    *abort = 0;
+    fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = p.lut[i];
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      prefetch_tmap(&mapQ);
+      prefetch_tmap(&mapK);
+      prefetch_tmap(&mapV);
+      bool ok = true;
+      mbar_arrive_expect_tx(qfull, Cfg::Q_BYTES);
+      tma_load_4d(smem + Cfg::OFF_Q, &mapQ, 0, h, q0, b, qfull);
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int st = j % Cfg::KS;
+        if (!mbar_wait(&kempty[st], ((j / Cfg::KS) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
+        mbar_arrive_expect_tx(&kfull[st], Cfg::K_BYTES);
+        tma_load_4d(smem + Cfg::OFF_K + st * Cfg::K_BYTES, &mapK, 0, h, j * 128, b, &kfull[st]);
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int st = j % Cfg::VS;
+        if (!mbar_wait(&vempty[st], ((j / Cfg::VS) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
+        mbar_arrive_expect_tx(&vfull[st], Cfg::V_BYTES);
+        tma_load_2d(smem + Cfg::OFF_V + st * Cfg::V_BYTES, &mapV, j * 128, bh * HD, &vfull[st]);
+      }
+      if (!ok) {              // aborted: let the copies already issued land before the CTA exits
+        mbar_wait_ns(qfull, 0, 10000000ull);
+        for (int s = 0; s < Cfg::KS; ++s) mbar_wait_ns(&kfull[s], 0, 10000000ull);
+        for (int s = 0; s < Cfg::VS; ++s) mbar_wait_ns(&vfull[s], 0, 10000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_qk = idesc_i8(128, 128);
+      constexpr uint32_t idesc_pv = idesc_i8(128, HD);
+      const uint32_t sq = smem_u32(smem + Cfg::OFF_Q);
+      bool ok = mbar_wait(qfull, 0, abort, p.flags, p.op_index);
+      tc_fence_after();
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int sb = j & 1, st = j % Cfg::KS;
+        if (!mbar_wait(&sempty[sb], ((j >> 1) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
+        if (!mbar_wait(&kfull[st], (j / Cfg::KS) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sk = smem_u32(smem + Cfg::OFF_K + st * Cfg::K_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < HD / 32; ++kk)
+          mma_i8(tmem + sb * 128, kmajor_desc(sq + 32 * kk, Cfg::QK_LAYOUT, Cfg::QK_SBO),
+                 kmajor_desc(sk + 32 * kk, Cfg::QK_LAYOUT, Cfg::QK_SBO), idesc_qk, kk > 0 ? 1u : 0u);
+        mma_commit(&kempty[st]);
+        mma_commit(&sfull[sb]);
+      }
+      if (ok) ok = mbar_wait(pready, 0, abort, p.flags, p.op_index);
+      tc_fence_after();
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int st = j % Cfg::VS;
+        if (!mbar_wait(&vfull[st], (j / Cfg::VS) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sp = smem_u32(pbuf + j * Cfg::P_SLAB);
+        const uint32_t sv = smem_u32(smem + Cfg::OFF_V + st * Cfg::V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_i8(tmem + 256, kmajor_desc(sp + 32 * kk, 2u, 1024u), kmajor_desc(sv + 32 * kk, 2u, 1024u), idesc_pv,
+                 (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&vempty[st]);
+      }
+      if (ok) mma_commit(ofull);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps: thread = query row
+    const int lane_base = 32 * (warp & 3);
+    const int r = lane_base + lane;
+    const int row = q0 + r;
+    const int kept = p.causal ? min(row + 1, p.T2) : p.T2;
+    const long long rnd1 = round_term(p.s1);
+    int mx = -128;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&sfull[sb], (j >> 1) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        int32_t acc[32];
+        __syncwarp();
+        tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(sb * 128 + c * 32), acc);
+        uint32_t w[8];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          const int col = j * 128 + c * 32 + q;
+          const int v = clampi(((long long)acc[q] * p.m1 + rnd1) >> p.s1, -128, 127);
+          if (col < kept) mx = max(mx, v);
+          if ((q & 3) == 0) w[q >> 2] = 0;
+          w[q >> 2] |= ((uint32_t)(uint8_t)v) << (8 * (q & 3));
+        }
+        uint8_t *slab = pbuf + j * Cfg::P_SLAB;
+        *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * c)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * c + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+      tc_fence_before();
+      mbar_arrive(&sempty[sb]);
+    }
+    // pass A: S = sum over kept columns of lut[x - max + 255]
+    long long tot = 0;
+    const int base_idx = 255 - mx;
+    if (ok) {
+      for (int j = 0; j < nkv; ++j) {
+        const uint8_t *slab = pbuf + j * Cfg::P_SLAB;
+#pragma unroll 1
+        for (int ch = 0; ch < 8; ++ch) {
+          const int c0 = j * 128 + ch * 16;
+          if (c0 >= kept) break;
+          const uint4 v4 = *reinterpret_cast<const uint4 *>(slab + pslab_off(r, ch));
+          const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const int x = (int8_t)((wv[q >> 2] >> (8 * (q & 3))) & 0xff);
+            if (c0 + q < kept) tot += lut[x + base_idx];
+          }
+        }
+      }
+    }
+    // pass B: p = floor((e*one + S/2) / S), masked entries 0; float reciprocal + one exact correction step
+    const int S = tot > 0 ? (int)tot : 1;
+    const int half = (int)(tot >> 1);
+    const float rS = 1.0f / (float)S;
+    if (ok) {
+      for (int j = 0; j < nkv; ++j) {
+        uint8_t *slab = pbuf + j * Cfg::P_SLAB;
+#pragma unroll 1
+        for (int ch = 0; ch < 8; ++ch) {
+          const int c0 = j * 128 + ch * 16;
+          uint4 v4 = *reinterpret_cast<const uint4 *>(slab + pslab_off(r, ch));
+          uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
+          uint32_t ov[4] = {0, 0, 0, 0};
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const int x = (int8_t)((wv[q >> 2] >> (8 * (q & 3))) & 0xff);
+            int pq = 0;
+            if (c0 + q < kept) {
+              const int num = lut[x + base_idx] * p.one + half;
+              int qq = (int)((float)num * rS);
+              const int rem = num - qq * S;
+              qq += (rem >= S) - (rem < 0);
+              pq = qq;
+            }
+            ov[q >> 2] |= ((uint32_t)(uint8_t)pq) << (8 * (q & 3));
+          }
+          *reinterpret_cast<uint4 *>(slab + pslab_off(r, ch)) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+        }
+      }
+    }
+    fence_proxy_async();
+    mbar_arrive(pready);
+    // O = P V from TMEM -> requant -> merged-heads output row
+    if (ok && mbar_wait(ofull, 0, abort, p.flags, p.op_index)) {
+      tc_fence_after();
+      const long long rnd2 = round_term(p.s2);
+      int8_t *orow = p.out + (int64_t)b * p.o_bs + (int64_t)row * p.o_rs + (int64_t)h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        int32_t acc[32];
+        __syncwarp();
+        tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(256 + c * 32), acc);
+        uint32_t w[8];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          const int v = clampi(((long long)acc[q] * p.m2 + rnd2) >> p.s2, -128, 127);
+          if ((q & 3) == 0) w[q >> 2] = 0;
+          w[q >> 2] |= ((uint32_t)(uint8_t)v) << (8 * (q & 3));
+        }
+        if (row < p.T1) {
+          uint4 *d4 = reinterpret_cast<uint4 *>(orow + c * 32);
+          d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace anvil

@@ -20,6 +20,8 @@ struct GemmParams {
   int64_t batch, M, N, K;
   int64_t a_bstride, bt_bstride;       // elements between batches (bt 0 = one weight for every batch)
   int64_t o_bstride, o_rstride;        // output elements between batches / rows
+  int64_t o_group, o_gstride;          // rows per output group (0: M) and elements between groups
+  int64_t o_cstride;                   // output elements between columns (1: row-major)
   const int8_t *A;
   const int8_t *BT;
   void *out;
@@ -100,7 +102,8 @@ __global__ void __launch_bounds__(256) qgemm_simt_kernel(GemmParams p) {
       int64_t gj = j0 + tx + 16 * r;
       if (gj >= p.N) continue;
       int v = gemm_epi<CHECK>(acc[q][r], p.bias ? p.bias[gj] : 0, p, lt, lo, hi, bad);
-      int64_t o = b * p.o_bstride + gi * p.o_rstride + gj;
+      const int64_t R = p.o_group ? p.o_group : p.M;
+      int64_t o = b * p.o_bstride + (gi / R) * p.o_gstride + (gi % R) * p.o_rstride + gj * p.o_cstride;
       if (p.out_bytes == 1) reinterpret_cast<int8_t *>(p.out)[o] = (int8_t)v;
       else reinterpret_cast<int16_t *>(p.out)[o] = (int16_t)v;
     }
@@ -272,7 +275,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int64_t row = mb * TC_BM + lane_base + lane;
       const bool row_ok = row < p.M;
       using TO = typename IntOf<OB>::T;
-      TO *orow = reinterpret_cast<TO *>(p.out) + bb * p.o_bstride + row * p.o_rstride;
+      const int64_t R = p.o_group ? p.o_group : p.M;
+      TO *orow = reinterpret_cast<TO *>(p.out) + bb * p.o_bstride + (row / R) * p.o_gstride + (row % R) * p.o_rstride;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         int32_t r[32];
@@ -290,7 +294,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int q = 0; q < 32; ++q)
               v[q] = gemm_epi<false>(r[q], (p.bias && col0 + q < p.N) ? p.bias[col0 + q] : 0, p, lt, lo, hi, bad);
           }
-          store_row32<OB>(orow + col0, v, (int)(p.N - col0 < 32 ? p.N - col0 : 32));
+          const int cnt = (int)(p.N - col0 < 32 ? p.N - col0 : 32);
+          if (p.o_cstride == 1) {
+            store_row32<OB>(orow + col0, v, cnt);
+          } else {            // strided columns (head-major transposed output): lanes = consecutive rows
+            TO *dst = orow + col0 * p.o_cstride;
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              if (q < cnt) dst[q * p.o_cstride] = (TO)v[q];
+          }
         }
       }
       tc_fence_before();

@@ -68,8 +68,10 @@ enum anvil_op_kind {
 
 /* One lowered kernel launch. Field meaning per kind (all sizes in elements, offsets in bytes):
  *   GEMM        dims  = {batch, M, N, K}; strides = {a_batch, bt_batch (0: shared weight), out_batch,
- *                       out_row}; off = {A (batch, M, K) int8, BT (batch|1, N, K) int8, OUT, LUT (256 i8),
- *                       BIAS (N i32)}; mult = M, shift = s; out_bytes = 1 (i8) or 2 (i16)
+ *                       out_row, out_group_rows (0: M), out_group, out_col (0: 1)}: element (b, row, col) goes to
+ *                       b*out_batch + (row / R)*out_group + (row % R)*out_row + col*out_col;
+ *                       off = {A (batch, M, K) int8, BT (batch|1, N, K) int8, OUT, LUT (256 i8), BIAS (N i32)};
+ *                       mult = M, shift = s; out_bytes = 1 (i8) or 2 (i16)
  *   LUT         dims  = {n}; off = {X, TABLE, OUT}
  *   LUT_MUL     dims  = {n}; off = {X, Y, TABLE, OUT}; mult, shift
  *   ADD_REQUANT dims  = {n}; off = {A, B, OUT}; in_bytes = a bytes, in2_bytes = b bytes, out_bytes;
@@ -80,9 +82,11 @@ enum anvil_op_kind {
  *   TRANSPOSE   dims  = {rank, n0, n1, n2, n3, n4, n5} (output dims); strides = input element strides per
  *               output dim; off = {X, OUT}; in_bytes = element bytes
  *   EMBED       dims  = {batch, T, d, vocab}; off = {IDS (i32), WTE, WPE, OUT}; ma, mb, shift
- *   ATTENTION   dims  = {batch, heads, T, hd}; strides = {q_row, k_row, v_row, o_row} (row = token stride,
- *               head h at column h*hd); off = {Q, K, V, OUT, EXP_LUT}; mult/shift = scores (M, s);
- *               ma/mb = p@v (M, s) packed as mult2 = ma, shift2 = mb; one; flags CAUSAL
+ *   ATTENTION   dims  = {B, H, T1, T2, hd (64 | 128)}; strides = {q_b, q_h, q_t, k_b, k_h, k_t, o_b, o_t}
+ *               (bytes; q element (b, h, t, d) at b*q_b + h*q_h + t*q_t + d, likewise k; the output element
+ *               (b, h, t, d) goes to b*o_b + t*o_t + h*hd + d, i.e. heads merged); off = {Q, K, VT, OUT, EXP_LUT}
+ *               with VT dense (B, H, hd, T2) (V transposed per head); mult/shift = scores (M, s),
+ *               mult2/shift2 = p@v (M, s); one (<= 127, i8 p); flags CAUSAL. T2 <= 1024, T2 % 16 == 0.
  *   COPY        dims  = {bytes}; off = {X, OUT}
  */
 typedef struct anvil_op {

@@ -49,6 +49,7 @@ class Emu:
     def k1(self, o):                                    # GEMM
         batch, M, N, K = (int(o.dims[i]) for i in range(4))
         abs_, bbs, obs, ors = (int(o.strides[i]) for i in range(4))
+        grp, gst, cst = int(o.strides[4]) or M, int(o.strides[5]), int(o.strides[6]) or 1
         lo, hi = RANGE[o.out_bytes]
         lut = self.get(o.off[3], 256, 1) if o.flags & C.F_LUT else None
         bias = self.get(o.off[4], N, 4) if o.flags & C.F_BIAS else None
@@ -61,8 +62,12 @@ class Emu:
             v = np.clip((acc * int(o.mult) + _rnd(int(o.shift))) >> int(o.shift), lo, hi)
             if lut is not None:
                 v = lut[v + 128]
-            for i in range(M):
-                self.put(o.off[2] + (b * obs + i * ors) * o.out_bytes, v[i], o.out_bytes)
+            mem, base = self._mem(o.off[2])
+            idx = (b * obs + (np.arange(M)[:, None] // grp) * gst + (np.arange(M)[:, None] % grp) * ors
+                   + np.arange(N)[None, :] * cst)
+            flat = mem[base:].view(DT[o.out_bytes])
+            assert idx.max() < flat.size, "write outside region"
+            flat[idx] = v.astype(DT[o.out_bytes])
 
     def k2(self, o):                                    # LUT
         n = int(o.dims[0])
@@ -136,6 +141,34 @@ class Emu:
         s = int(o.shift)
         v = (wte[ids] * int(o.ma) + wpe[None] * int(o.mb) + _rnd(s)) >> s
         self.put(o.off[3], np.clip(v, -128, 127), 1)
+
+    def k9(self, o):                                    # ATTENTION
+        B, H, T1, T2, hd = (int(o.dims[i]) for i in range(5))
+        st = [int(o.strides[i]) for i in range(8)]
+        lut = self.get(o.off[4], 256, 4)
+        mq, mk = self._mem(o.off[0]), self._mem(o.off[1])
+        vt = self.get(o.off[2], B * H * hd * T2, 1).reshape(B, H, hd, T2)
+        qv = mq[0][mq[1]:].view(np.int8)
+        kv = mk[0][mk[1]:].view(np.int8)
+        bi, hi, ti, di = np.ix_(np.arange(B), np.arange(H), np.arange(T1), np.arange(hd))
+        q = qv[bi * st[0] + hi * st[1] + ti * st[2] + di].astype(np.int64)
+        bi, hi, ti, di = np.ix_(np.arange(B), np.arange(H), np.arange(T2), np.arange(hd))
+        k = kv[bi * st[3] + hi * st[4] + ti * st[5] + di].astype(np.int64)
+        s1, s2 = int(o.shift), int(o.shift2)
+        sc = np.clip((q @ np.swapaxes(k, -1, -2) * int(o.mult) + _rnd(s1)) >> s1, -128, 127)
+        keep = np.ones((T1, T2), bool)
+        if o.flags & C.F_CAUSAL:
+            keep = np.arange(T2)[None, :] <= np.arange(T1)[:, None]
+        keep = np.broadcast_to(keep, sc.shape)
+        mx = np.maximum(np.where(keep, sc, -128).max(axis=-1, keepdims=True), -128)
+        e = np.where(keep, lut[np.where(keep, sc - mx + 255, 255)], 0)
+        tot = e.sum(axis=-1, keepdims=True)
+        p = np.where(keep, (e * int(o.one) + tot // 2) // np.maximum(tot, 1), 0)
+        out = np.clip((p @ np.swapaxes(vt, -1, -2) * int(o.mult2) + _rnd(s2)) >> s2, -128, 127)   # (B, H, T1, hd)
+        mem, base = self._mem(o.off[3])
+        bi, hi, ti, di = np.ix_(np.arange(B), np.arange(H), np.arange(T1), np.arange(hd))
+        flat = mem[base:].view(np.int8)
+        flat[bi * st[6] + ti * st[7] + hi * hd + di] = out.astype(np.int8)
 
     def k10(self, o):                                   # COPY
         n = int(o.dims[0])

@@ -156,3 +156,49 @@ def random_case(seed, big=False, ext=True, tries=60, batch=None):
         except (OverflowError, ValueError, ZeroDivisionError, IndexError):
             continue
     raise RuntimeError(f"seed {seed}: no in-contract draw in {tries} tries")
+
+
+def attention_graph(seed, T, C, nh, causal=True, T2=None):
+    """(module, consts, x) for x -> q/k/v projections -> heads -> qk^T -> softmax_lut -> p@v -> merged heads ->
+    projection: the chain the fused attention kernel runs (self-attention when T2 is None)."""
+    rng = np.random.default_rng(seed)
+    T2 = T if T2 is None else T2
+    hd = C // nh
+    g = GraphBuilder("attn")
+    consts = {}
+
+    def const(name, shape, dtype="i8", value=None):
+        v = rng.integers(-128, 128, shape) if value is None else np.asarray(value)
+        consts[name] = np.asarray(v, dtype=np.int64)
+        return g.const(name, list(np.shape(v)), dtype)
+
+    from anvil.frontend.numerics import fixed_point
+
+    def fp(gain, bound):                       # (M, s) that the static int32 proof accepts
+        (m,), s = fixed_point([gain * rng.uniform(0.7, 1.4)], [bound])
+        return m, s
+
+    def lin(name, x_, w_):
+        wv = rng.integers(-127, 128, (C, C))
+        return g.qlinear(name, x_, const(w_, [C, C], value=wv),
+                         *fp(40.0 / (ACT * 73 * np.sqrt(C)), 128 * int(np.abs(wv).sum(axis=0).max())))
+
+    x = g.input("x", [T, C])
+    xk = g.input("xk", [T2, C]) if T2 != T else x
+    q = lin("q", x, "wq")
+    k = lin("k", xk, "wk")
+    v = lin("v", xk, "wv")
+    qh = g.transpose("qh", g.reshape("q3", q, [T, nh, hd]), [1, 0, 2])
+    kh = g.transpose("kh", g.reshape("k3", k, [T2, nh, hd]), [1, 0, 2])
+    kT = g.transpose("kT", kh, [0, 2, 1])
+    sc = g.qmatmul("scores", qh, kT, *fp(30.0 / (40.0 * 40.0 * np.sqrt(hd)), hd * 128 * 128))
+    p = g.softmax_lut("p", sc, const("exp", [256], "i32", exp_lut(tau=12.0, e=14)), 127, causal)
+    vh = g.transpose("vh", g.reshape("v3", v, [T2, nh, hd]), [1, 0, 2])
+    o = g.qmatmul("o", p, vh, *fp(40.0 / (127 * 40.0 / np.sqrt(max(T2, 1)) * 3), T2 * 127 * 128))
+    om = g.reshape("om", g.transpose("om.t", o, [1, 0, 2]), [T, C])
+    y = lin("y", om, "wo")
+    g.output(y)
+    xs = {"x": rng.integers(-128, 128, (T, C))}
+    if T2 != T:
+        xs["xk"] = rng.integers(-128, 128, (T2, C))
+    return g.module(), consts, xs

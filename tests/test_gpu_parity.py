@@ -159,3 +159,38 @@ def test_embed_index_error():
     _check(cm.run(ok, "cuda", quantized=True).ints, interp.run(m, {"ids": ok}, c).values, consts=c)
     with pytest.raises(IndexError):
         cm.run(np.array([0, 3, 10, 2, 2, 1]), "cuda", quantized=True)
+
+
+# ------------------------------------------------------------------------------------------ fused attention
+
+@pytest.mark.parametrize("T,C,nh,causal,T2", [(256, 128, 2, True, None), (128, 128, 2, False, None),
+                                              (208, 256, 2, True, None), (1024, 768, 12, True, None),
+                                              (96, 128, 2, False, 160), (64, 512, 4, True, None),
+                                              (200, 128, 2, True, None)])
+def test_fused_attention_bit_exact(T, C, nh, causal, T2):
+    from graphs import attention_graph
+    m, c, x = attention_graph(T + C + nh, T, C, nh, causal, T2)
+    batch = 2
+    rng = np.random.default_rng(7)
+    xb = {k: np.stack([v] + [rng.integers(-128, 128, v.shape) for _ in range(batch - 1)]) for k, v in x.items()}
+    want = interp.run(m, xb, c, batch=True)
+    cm = anvil.compile(m, consts=c)
+    prog = cm.program(batch)
+    fusable = (C // nh) in (64, 128) and (T2 or T) % 16 == 0
+    assert any("attention" in f for f in prog.fused) == fusable
+    res = cm.run([xb[s] for s in cm.inputs], "cuda", quantized=True)
+    _check(res.ints, want.values, cm.outputs)
+    unfused = anvil.compile(m, consts=c, params=CudaParams(fuse=False))
+    _check(unfused.run([xb[s] for s in cm.inputs], "cuda", quantized=True).ints, want.values, cm.outputs)
+
+
+def test_c3_block_fused_matches_oracle():
+    """Config c3 (GPT-2-small int8 block, T 1024) through the torch frontend: 2 sequences on the GPU vs the oracle."""
+    from anvil import workloads as W
+    cm, gen = W.compile_config("c3")
+    x = gen(2)
+    xq = cm.quantize_input(x)
+    want = interp.run(cm.module, {cm.inputs[0]: xq}, cm.consts, batch=True)
+    res = cm.run(xq, "cuda", quantized=True)
+    assert any("attention" in f for f in res.job.fused)
+    _check(res.ints, want.values, cm.outputs)
