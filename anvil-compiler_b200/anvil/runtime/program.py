@@ -348,7 +348,14 @@ class Lowering:
             flags |= C.F_LUT
         bias_slot = None
         if op.bias is not None:
-            bias_slot = self.const_slot(self.views[id(op.bias)], np.int32)
+            bv = self.views[id(op.bias)]
+            if self.checked:
+                bias_slot = self.const_slot(bv, np.int32)
+            else:                   # proven: fold the bias into the rounding term, bias*M + 2^(s-1)
+                folded = self.const_array(bv) * int(op.M) + ((1 << (op.s - 1)) if op.s else 0)
+                bias_slot = ("const", self.pool.add((bv.root, "bias_rnd", int(op.M), int(op.s)),
+                                                    np.ascontiguousarray(folded, dtype=np.int32)))
+                flags |= C.F_BIAS_RND
             flags |= C.F_BIAS
         reads = [a.root]
         if b.const and len(b.shape) == 2:

@@ -274,6 +274,9 @@ static int prepare_gemm(anvil_model *m, Launch &L) {
   p.out = L.ptr[2];
   p.lut = (op.flags & ANVIL_F_LUT) ? (const int8_t *)L.ptr[3] : nullptr;
   p.bias = (op.flags & ANVIL_F_BIAS) ? (const int32_t *)L.ptr[4] : nullptr;
+  if (p.bias && (((op.flags & ANVIL_F_BIAS_RND) != 0) == ((op.flags & ANVIL_F_CHECKED) != 0)))
+    return fail(ANVIL_E_BAD_ARG, "op %d: a checked gemm takes a raw bias, an unchecked one a folded bias*M + round",
+                op.op_index);
   p.mult = op.mult;
   p.shift = (int)op.shift;
   p.out_bytes = op.out_bytes;
@@ -551,9 +554,9 @@ static int launch_op(anvil_model *m, Launch &L) {
       const int64_t grid = (int64_t)a.B * a.H * a.nqt;
       if (grid > 0x7fffffff) return fail(ANVIL_E_BAD_ARG, "op %d: attention grid too large", oi);
       if (L.hd == 64)
-        attn_kernel<64><<<(unsigned)grid, 192, AttnCfg<64>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, a);
+        attn_kernel<64><<<(unsigned)grid, ATTN_THREADS, AttnCfg<64>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, a);
       else
-        attn_kernel<128><<<(unsigned)grid, 192, AttnCfg<128>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, a);
+        attn_kernel<128><<<(unsigned)grid, ATTN_THREADS, AttnCfg<128>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, a);
       break;
     }
     default:

@@ -4,14 +4,17 @@
 //   o      = requant(p @ v, M2, s2), written straight into the merged-heads layout (b, t, h*hd + d)
 //
 // One CTA per (batch, head, 128-query tile), heaviest causal tiles first. Warp roles:
-//   warp 0     TMA: the Q tile once, then K tiles (128 keys x hd) into a KS-deep ring, then V^T slabs
-//              (hd x 128 keys, from the head-major transposed V the v-projection GEMM writes) into a VS-deep ring
+//   warp 0     TMA: the Q tile once, then through one NS-deep ring the K tiles (128 keys x hd) and after them
+//              the V^T slabs (hd x 128 keys, from the head-major transposed V the v-projection GEMM writes), so the
+//              V loads land while the softmax runs
 //   warp 1     tcgen05.mma kind::i8: S_j = Q K_j^T into one of two TMEM buffers (128 x 128 int32); after the
 //              softmax, O = sum_j P_j V_j into a third TMEM region (128 x hd)
-//   warps 2-5  one thread per query row: drain S_j from TMEM, requant to int8, track the row max, store the row
-//              into the P slab j in shared memory (the 128-byte-swizzled K-major layout the P @ V MMA reads);
-//              then the two exact softmax passes over the slabs (sum of exp_lut, then (e*one + S/2) / S by a
-//              float reciprocal with an integer correction step), then O from TMEM -> requant -> global
+//   warps 2-17 four threads per query row, each owning a 32-column part of every 128-key slab: drain S_j from
+//              TMEM, requant to int8, track the partial row max, store into the P slab j in shared memory (the
+//              128-byte-swizzled K-major layout the P @ V MMA reads); combine the row max across the four parts,
+//              then the two exact softmax passes (partial sums of exp_lut combined the same way, then
+//              (e*one + S/2) / S by a float reciprocal with an integer correction step), then O from TMEM ->
+//              requant -> global
 // The whole score row (up to 1024 keys, int8) stays in shared memory, so the row max and row sum are exact before
 // any probability is formed, as the reference's three-stage loop nest requires; an online (rescaled) softmax
 // would not be bit-exact.
@@ -34,20 +37,19 @@ struct AttnParams {
 
 template <int HD>
 struct AttnCfg {
-  static constexpr int KS = HD == 64 ? 3 : 2;
-  static constexpr int VS = HD == 64 ? 3 : 2;
+  static constexpr int NS = HD == 64 ? 6 : 4;           // one ring for K tiles then V^T slabs (same size)
+  static constexpr int LUT_COPIES = HD == 64 ? 32 : 8;  // exp LUT replicated per lane: conflict-free lookups
   static constexpr int Q_BYTES = 128 * HD;
-  static constexpr int K_BYTES = 128 * HD;
-  static constexpr int V_BYTES = HD * 128;
+  static constexpr int T_BYTES = 128 * HD;              // a K tile (128 keys x hd) or a V^T slab (hd x 128 keys)
   static constexpr int MAX_SLABS = 8;                   // T2 <= 1024
   static constexpr int P_SLAB = 128 * 128;
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + Q_BYTES;
-  static constexpr int OFF_V = OFF_K + KS * K_BYTES;
-  static constexpr int OFF_P = OFF_V + VS * V_BYTES;
+  static constexpr int OFF_R = OFF_Q + Q_BYTES;
+  static constexpr int OFF_P = OFF_R + NS * T_BYTES;
   static constexpr int OFF_LUT = OFF_P + MAX_SLABS * P_SLAB;
-  static constexpr int OFF_BAR = OFF_LUT + 1024;
-  static constexpr int NBAR = 1 + 2 * KS + 2 * VS + 2 + 2 + 1 + 1;
+  static constexpr int OFF_RED = OFF_LUT + 1024 * LUT_COPIES;       // [4][128] int32 row partials
+  static constexpr int OFF_BAR = OFF_RED + 2048;
+  static constexpr int NBAR = 1 + 2 * NS + 2 + 2 + 1 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   // Q / K tiles: rows of HD bytes. 64-byte rows use the 64-byte swizzle (8-row atoms of 512 B), 128-byte rows
@@ -88,8 +90,11 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 // byte offset of 16-byte chunk `ch` (0..7) of row `r` (0..127) inside one 128 x 128 P slab (SW128 K-major)
 __device__ __forceinline__ int pslab_off(int r, int ch) { return (r >> 3) * 1024 + (r & 7) * 128 + ((ch ^ (r & 7)) << 4); }
 
+constexpr int ATTN_SOFTMAX_THREADS = 512;                 // 16 warps: 4 threads per query row
+constexpr int ATTN_THREADS = 64 + ATTN_SOFTMAX_THREADS;
+
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(ATTN_THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                 const __grid_constant__ CUtensorMap mapV, const AttnParams p) {
   using Cfg = AttnCfg<HD>;
@@ -97,13 +102,12 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::OFF_BAR);
   uint64_t *qfull = bars;
-  uint64_t *kfull = qfull + 1, *kempty = kfull + Cfg::KS;
-  uint64_t *vfull = kempty + Cfg::KS, *vempty = vfull + Cfg::VS;
-  uint64_t *sfull = vempty + Cfg::VS, *sempty = sfull + 2;
+  uint64_t *rfull = qfull + 1, *rempty = rfull + Cfg::NS;
+  uint64_t *sfull = rempty + Cfg::NS, *sempty = sfull + 2;
   uint64_t *pready = sempty + 2, *ofull = pready + 1;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Cfg::OFF_MISC);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + Cfg::OFF_MISC + 4);
-  int32_t *lut = reinterpret_cast<int32_t *>(smem + Cfg::OFF_LUT);
+  int32_t *lut = reinterpret_cast<int32_t *>(smem + Cfg::OFF_LUT);   // entry i of copy c at word i*COPIES + c
   uint8_t *pbuf = smem + Cfg::OFF_P;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -117,15 +121,14 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(qfull, 1);
-    for (int i = 0; i < Cfg::KS; ++i) { mbar_init(&kfull[i], 1); mbar_init(&kempty[i], 1); }
-    for (int i = 0; i < Cfg::VS; ++i) { mbar_init(&vfull[i], 1); mbar_init(&vempty[i], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&sfull[i], 1); mbar_init(&sempty[i], 128); }
-    mbar_init(pready, 128);
+    for (int i = 0; i < Cfg::NS; ++i) { mbar_init(&rfull[i], 1); mbar_init(&rempty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&sfull[i], 1); mbar_init(&sempty[i], ATTN_SOFTMAX_THREADS); }
+    mbar_init(pready, ATTN_SOFTMAX_THREADS);
     mbar_init(ofull, 1);
     *abort = 0;
     fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = p.lut[i];
+  for (int i = threadIdx.x; i < 256 * Cfg::LUT_COPIES; i += blockDim.x) lut[i] = p.lut[i / Cfg::LUT_COPIES];
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
@@ -140,22 +143,21 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       mbar_arrive_expect_tx(qfull, Cfg::Q_BYTES);
       tma_load_4d(smem + Cfg::OFF_Q, &mapQ, 0, h, q0, b, qfull);
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int st = j % Cfg::KS;
-        if (!mbar_wait(&kempty[st], ((j / Cfg::KS) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
-        mbar_arrive_expect_tx(&kfull[st], Cfg::K_BYTES);
-        tma_load_4d(smem + Cfg::OFF_K + st * Cfg::K_BYTES, &mapK, 0, h, j * 128, b, &kfull[st]);
-      }
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int st = j % Cfg::VS;
-        if (!mbar_wait(&vempty[st], ((j / Cfg::VS) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
-        mbar_arrive_expect_tx(&vfull[st], Cfg::V_BYTES);
-        tma_load_2d(smem + Cfg::OFF_V + st * Cfg::V_BYTES, &mapV, j * 128, bh * HD, &vfull[st]);
+      // ring sequence g: K tiles 0..nkv-1, then V^T slabs 0..nkv-1 (the V loads land while the softmax runs)
+      for (int g = 0; g < 2 * nkv && ok; ++g) {
+        const int st = g % Cfg::NS;
+        if (!mbar_wait(&rempty[st], ((g / Cfg::NS) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
+        mbar_arrive_expect_tx(&rfull[st], Cfg::T_BYTES);
+        uint8_t *dst = smem + Cfg::OFF_R + st * Cfg::T_BYTES;
+        if (g < nkv) tma_load_4d(dst, &mapK, 0, h, g * 128, b, &rfull[st]);
+        else tma_load_2d(dst, &mapV, (g - nkv) * 128, bh * HD, &rfull[st]);
       }
       if (!ok) {              // aborted: let the copies already issued land before the CTA exits
         mbar_wait_ns(qfull, 0, 10000000ull);
-        for (int s = 0; s < Cfg::KS; ++s) mbar_wait_ns(&kfull[s], 0, 10000000ull);
-        for (int s = 0; s < Cfg::VS; ++s) mbar_wait_ns(&vfull[s], 0, 10000000ull);
+        for (int s2 = 0; s2 < Cfg::NS; ++s2) {
+          mbar_wait_ns(&rfull[s2], 0, 10000000ull);
+          mbar_wait_ns(&rfull[s2], 1, 10000000ull);
+        }
       }
     }
   } else if (warp == 1) {
@@ -166,142 +168,149 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = mbar_wait(qfull, 0, abort, p.flags, p.op_index);
       tc_fence_after();
       for (int j = 0; j < nkv && ok; ++j) {
-        const int sb = j & 1, st = j % Cfg::KS;
+        const int sb = j & 1, st = j % Cfg::NS;
         if (!mbar_wait(&sempty[sb], ((j >> 1) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
-        if (!mbar_wait(&kfull[st], (j / Cfg::KS) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
+        if (!mbar_wait(&rfull[st], (j / Cfg::NS) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sk = smem_u32(smem + Cfg::OFF_K + st * Cfg::K_BYTES);
+        const uint32_t sk = smem_u32(smem + Cfg::OFF_R + st * Cfg::T_BYTES);
 #pragma unroll
         for (int kk = 0; kk < HD / 32; ++kk)
           mma_i8(tmem + sb * 128, kmajor_desc(sq + 32 * kk, Cfg::QK_LAYOUT, Cfg::QK_SBO),
                  kmajor_desc(sk + 32 * kk, Cfg::QK_LAYOUT, Cfg::QK_SBO), idesc_qk, kk > 0 ? 1u : 0u);
-        mma_commit(&kempty[st]);
+        mma_commit(&rempty[st]);
         mma_commit(&sfull[sb]);
       }
       if (ok) ok = mbar_wait(pready, 0, abort, p.flags, p.op_index);
       tc_fence_after();
       for (int j = 0; j < nkv && ok; ++j) {
-        const int st = j % Cfg::VS;
-        if (!mbar_wait(&vfull[st], (j / Cfg::VS) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
+        const int g = nkv + j, st = g % Cfg::NS;
+        if (!mbar_wait(&rfull[st], (g / Cfg::NS) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sp = smem_u32(pbuf + j * Cfg::P_SLAB);
-        const uint32_t sv = smem_u32(smem + Cfg::OFF_V + st * Cfg::V_BYTES);
+        const uint32_t sv = smem_u32(smem + Cfg::OFF_R + st * Cfg::T_BYTES);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_i8(tmem + 256, kmajor_desc(sp + 32 * kk, 2u, 1024u), kmajor_desc(sv + 32 * kk, 2u, 1024u), idesc_pv,
                  (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&vempty[st]);
+        mma_commit(&rempty[st]);
       }
       if (ok) mma_commit(ofull);
     }
   } else {
-    // ------------------------------------------------------------ softmax warps: thread = query row
-    const int lane_base = 32 * (warp & 3);
+    // -------------------------------------------- softmax warps: 4 threads per query row, one 32-column part each
+    const int lane_base = 32 * (warp & 3);           // TMEM lanes this warp may read
+    const int part = (warp - 2) >> 2;                // 0..3: columns [32*part, 32*part + 32) of every slab
     const int r = lane_base + lane;
     const int row = q0 + r;
     const int kept = p.causal ? min(row + 1, p.T2) : p.T2;
-    const long long rnd1 = round_term(p.s1);
+    const int m1 = (int)p.m1;
+    const int rnd1 = (int)round_term(p.s1);
+    int32_t *red = reinterpret_cast<int32_t *>(smem + Cfg::OFF_RED);   // [4][128] partial max / sum per row
+    const int lcopy = lane % Cfg::LUT_COPIES;
     int mx = -128;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int sb = j & 1;
-      if (!mbar_wait(&sfull[sb], (j >> 1) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
+      ok = __all_sync(0xffffffffu, mbar_wait(&sfull[sb], (j >> 1) & 1, abort, p.flags, p.op_index));
+      if (!ok) break;                       // warp-uniform: the TMEM load below is .sync.aligned
       tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        int32_t acc[32];
-        __syncwarp();
-        tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(sb * 128 + c * 32), acc);
-        uint32_t w[8];
+      int32_t acc[32];
+      tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(sb * 128 + part * 32), acc);
+      uint32_t w[8];
+      const int cbase = j * 128 + part * 32;
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const int col = j * 128 + c * 32 + q;
-          const int v = clampi(((long long)acc[q] * p.m1 + rnd1) >> p.s1, -128, 127);
-          if (col < kept) mx = max(mx, v);
-          if ((q & 3) == 0) w[q >> 2] = 0;
-          w[q >> 2] |= ((uint32_t)(uint8_t)v) << (8 * (q & 3));
-        }
-        uint8_t *slab = pbuf + j * Cfg::P_SLAB;
-        *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * c)) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * c + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+      for (int q = 0; q < 32; ++q) {
+        // the static int32 proof holds on this path: acc*M1 + 2^(s1-1) fits int32
+        const int v = min(127, max(-128, (acc[q] * m1 + rnd1) >> p.s1));
+        if (cbase + q < kept) mx = max(mx, v);
+        if ((q & 3) == 0) w[q >> 2] = 0;
+        w[q >> 2] |= ((uint32_t)(uint8_t)v) << (8 * (q & 3));
       }
+      uint8_t *slab = pbuf + j * Cfg::P_SLAB;
+      *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part)) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
       tc_fence_before();
       mbar_arrive(&sempty[sb]);
     }
-    // pass A: S = sum over kept columns of lut[x - max + 255]
-    long long tot = 0;
+    // row max over the 4 parts
+    red[part * 128 + r] = mx;
+    asm volatile("bar.sync 1, 512;" ::: "memory");
+    mx = max(max(red[r], red[128 + r]), max(red[256 + r], red[384 + r]));
+    asm volatile("bar.sync 1, 512;" ::: "memory");
     const int base_idx = 255 - mx;
-    if (ok) {
-      for (int j = 0; j < nkv; ++j) {
-        const uint8_t *slab = pbuf + j * Cfg::P_SLAB;
-#pragma unroll 1
-        for (int ch = 0; ch < 8; ++ch) {
-          const int c0 = j * 128 + ch * 16;
-          if (c0 >= kept) break;
-          const uint4 v4 = *reinterpret_cast<const uint4 *>(slab + pslab_off(r, ch));
+    // pass A: partial S = sum over this part's kept columns of lut[x - max + 255]
+    int tot = 0;
+    for (int j = 0; j < nkv && ok; ++j) {
+      const uint8_t *slab = pbuf + j * Cfg::P_SLAB;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int c0 = j * 128 + part * 32 + hh * 16;
+        if (c0 < kept) {
+          const uint4 v4 = *reinterpret_cast<const uint4 *>(slab + pslab_off(r, 2 * part + hh));
           const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            const int x = (int8_t)((wv[q >> 2] >> (8 * (q & 3))) & 0xff);
-            if (c0 + q < kept) tot += lut[x + base_idx];
+            const int x = (int)(int8_t)(wv[q >> 2] >> (8 * (q & 3)));
+            if (c0 + q < kept) tot += lut[(x + base_idx) * Cfg::LUT_COPIES + lcopy];
           }
         }
       }
     }
+    red[part * 128 + r] = tot;
+    asm volatile("bar.sync 1, 512;" ::: "memory");
+    tot = red[r] + red[128 + r] + red[256 + r] + red[384 + r];
     // pass B: p = floor((e*one + S/2) / S), masked entries 0; float reciprocal + one exact correction step
-    const int S = tot > 0 ? (int)tot : 1;
-    const int half = (int)(tot >> 1);
+    const int S = tot > 0 ? tot : 1;
+    const int half = tot >> 1;
     const float rS = 1.0f / (float)S;
-    if (ok) {
-      for (int j = 0; j < nkv; ++j) {
-        uint8_t *slab = pbuf + j * Cfg::P_SLAB;
-#pragma unroll 1
-        for (int ch = 0; ch < 8; ++ch) {
-          const int c0 = j * 128 + ch * 16;
-          uint4 v4 = *reinterpret_cast<const uint4 *>(slab + pslab_off(r, ch));
-          uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
-          uint32_t ov[4] = {0, 0, 0, 0};
+    const int one = p.one;
+    for (int j = 0; j < nkv && ok; ++j) {
+      uint8_t *slab = pbuf + j * Cfg::P_SLAB;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int c0 = j * 128 + part * 32 + hh * 16;
+        const int off = pslab_off(r, 2 * part + hh);
+        uint4 v4 = *reinterpret_cast<const uint4 *>(slab + off);
+        const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
+        uint32_t ov[4] = {0, 0, 0, 0};
+        if (c0 < kept) {
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            const int x = (int8_t)((wv[q >> 2] >> (8 * (q & 3))) & 0xff);
+            const int x = (int)(int8_t)(wv[q >> 2] >> (8 * (q & 3)));
             int pq = 0;
             if (c0 + q < kept) {
-              const int num = lut[x + base_idx] * p.one + half;
-              int qq = (int)((float)num * rS);
+              const int num = lut[(x + base_idx) * Cfg::LUT_COPIES + lcopy] * one + half;
+              int qq = __float2int_rz((float)num * rS);
               const int rem = num - qq * S;
               qq += (rem >= S) - (rem < 0);
               pq = qq;
             }
             ov[q >> 2] |= ((uint32_t)(uint8_t)pq) << (8 * (q & 3));
           }
-          *reinterpret_cast<uint4 *>(slab + pslab_off(r, ch)) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
         }
+        *reinterpret_cast<uint4 *>(slab + off) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
       }
     }
     fence_proxy_async();
     mbar_arrive(pready);
-    // O = P V from TMEM -> requant -> merged-heads output row
-    if (ok && mbar_wait(ofull, 0, abort, p.flags, p.op_index)) {
+    // O = P V from TMEM -> requant -> merged-heads output row (parts 0 .. HD/32-1 take 32 columns each)
+    if (ok && part < HD / 32 && __all_sync(0xffffffffu, mbar_wait(ofull, 0, abort, p.flags, p.op_index))) {
       tc_fence_after();
       const long long rnd2 = round_term(p.s2);
-      int8_t *orow = p.out + (int64_t)b * p.o_bs + (int64_t)row * p.o_rs + (int64_t)h * HD;
-#pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        int32_t acc[32];
-        __syncwarp();
-        tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(256 + c * 32), acc);
-        uint32_t w[8];
+      int32_t acc[32];
+      tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(256 + part * 32), acc);
+      uint32_t w[8];
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const int v = clampi(((long long)acc[q] * p.m2 + rnd2) >> p.s2, -128, 127);
-          if ((q & 3) == 0) w[q >> 2] = 0;
-          w[q >> 2] |= ((uint32_t)(uint8_t)v) << (8 * (q & 3));
-        }
-        if (row < p.T1) {
-          uint4 *d4 = reinterpret_cast<uint4 *>(orow + c * 32);
-          d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        }
+      for (int q = 0; q < 32; ++q) {
+        const int v = clampi(((long long)acc[q] * p.m2 + rnd2) >> p.s2, -128, 127);
+        if ((q & 3) == 0) w[q >> 2] = 0;
+        w[q >> 2] |= ((uint32_t)(uint8_t)v) << (8 * (q & 3));
+      }
+      if (row < p.T1) {
+        int8_t *orow = p.out + (int64_t)b * p.o_bs + (int64_t)row * p.o_rs + (int64_t)h * HD + part * 32;
+        uint4 *d4 = reinterpret_cast<uint4 *>(orow);
+        d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
       }
     }
   }

@@ -101,7 +101,13 @@ __global__ void __launch_bounds__(256) qgemm_simt_kernel(GemmParams p) {
     for (int r = 0; r < 4; ++r) {
       int64_t gj = j0 + tx + 16 * r;
       if (gj >= p.N) continue;
-      int v = gemm_epi<CHECK>(acc[q][r], p.bias ? p.bias[gj] : 0, p, lt, lo, hi, bad);
+      int v;
+      if (CHECK || !p.bias) {
+        v = gemm_epi<CHECK>(acc[q][r], p.bias ? p.bias[gj] : 0, p, lt, lo, hi, bad);
+      } else {                  // bias folded as bias*M + 2^(s-1) (ANVIL_F_BIAS_RND)
+        v = clampi(((long long)acc[q][r] * p.mult + p.bias[gj]) >> p.shift, lo, hi);
+        if (lt) v = lt[v + 128];
+      }
       const int64_t R = p.o_group ? p.o_group : p.M;
       int64_t o = b * p.o_bstride + (gi / R) * p.o_gstride + (gi % R) * p.o_rstride + gj * p.o_cstride;
       if (p.out_bytes == 1) reinterpret_cast<int8_t *>(p.out)[o] = (int8_t)v;
@@ -115,7 +121,8 @@ __global__ void __launch_bounds__(256) qgemm_simt_kernel(GemmParams p) {
 
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 128;                // bytes of K per stage = one 128-byte swizzle row
-constexpr int TC_THREADS = 192;           // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int TC_EPI_WARPS = 8;           // two warps per TMEM lane quarter, each owning half the tile's columns
+constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int TC_SMEM_RING = 192 * 1024;  // bytes of A/B stages
 
 template <int BN>
@@ -125,10 +132,13 @@ struct TcCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = TC_SMEM_RING / STAGE_BYTES > 8 ? 8 : TC_SMEM_RING / STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;     // two accumulators
-  // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2]; then the TMEM base slot, abort word, LUT
+  // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2]; then the TMEM base slot and abort word, the LUT
+  // replicated once per lane (8 KB, conflict-free lookups), and a 128-byte bias staging slot per epilogue warp
   static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
   static constexpr int MISC_OFF = BAR_OFF + (2 * STAGES + 4) * 8;
-  static constexpr int SMEM_BYTES = MISC_OFF + 16 + 256 + 1024;   // + 1 KB slack to align the ring to 1024 B
+  static constexpr int LUT_OFF = MISC_OFF + 16;
+  static constexpr int BST_OFF = LUT_OFF + 32 * 256;
+  static constexpr int SMEM_BYTES = BST_OFF + TC_EPI_WARPS * 128 + 1024;   // + 1 KB slack to align the ring
 };
 
 // Store 32 consecutive results of one output row: 16-byte vector stores when the whole chunk is in range and
@@ -173,7 +183,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t *tempty = tfull + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Cfg::MISC_OFF);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + Cfg::MISC_OFF + 4);
-  int8_t *lut_s = reinterpret_cast<int8_t *>(smem + Cfg::MISC_OFF + 16);
+  int8_t *lut_r = reinterpret_cast<int8_t *>(smem + Cfg::LUT_OFF);      // entry i of lane l's copy: (i/4)*128 + 4l + i%4
+  int32_t *bst = reinterpret_cast<int32_t *>(smem + Cfg::BST_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -183,7 +194,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
+      mbar_init(&tempty[i], 32 * TC_EPI_WARPS);
     }
     *abort = 0;
     fence_mbar_init();
@@ -193,7 +204,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     prefetch_tmap(&tmB);
   }
   if (p.lut)
-    for (int i = threadIdx.x; i < 256; i += TC_THREADS) lut_s[i] = p.lut[i];
+    for (int i = threadIdx.x; i < 32 * 256; i += TC_THREADS) {
+      const int e = i & 255, l = i >> 8;
+      lut_r[(e >> 2) * 128 + l * 4 + (e & 3)] = p.lut[e];
+    }
   if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
@@ -259,18 +273,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    // ------------------------------------------------------------------ epilogue (warps 2..9)
+    // warp w reads TMEM lane quarter (w % 4) and columns [half*BN/2, half*BN/2 + BN/2), half = (w - 2) / 4
     const int lane_base = 32 * (warp & 3);
+    const int half = (warp - 2) >> 2;
+    int32_t *bslot = bst + (warp - 2) * 32;
     int acc = 0;
     uint32_t aphase = 0;
-    int lo, hi;
-    if (OB == 1) { lo = -128; hi = 127; } else { lo = -32768; hi = 32767; }
-    const int8_t *lt = p.lut ? lut_s : nullptr;
+    constexpr int lo = OB == 1 ? -128 : -32768, hi = OB == 1 ? 127 : 32767;
+    const int8_t *lt = p.lut ? lut_r : nullptr;
+    const int m32 = (int)p.mult, sh = p.shift, rnd = sh ? 1 << (sh - 1) : 0;
     bool bad = false;
     for (int64_t t = blockIdx.x; t < p.tiles; t += gridDim.x) {
       const int64_t nb = t % p.n_tiles, rest = t / p.n_tiles;
       const int64_t mb = rest % p.m_tiles, bb = rest / p.m_tiles;
-      if (!mbar_wait(&tfull[acc], aphase, abort, p.flags, p.op_index)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aphase, abort, p.flags, p.op_index))) break;
       tc_fence_after();
       const int64_t row = mb * TC_BM + lane_base + lane;
       const bool row_ok = row < p.M;
@@ -278,22 +295,46 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int64_t R = p.o_group ? p.o_group : p.M;
       TO *orow = reinterpret_cast<TO *>(p.out) + bb * p.o_bstride + (row / R) * p.o_gstride + (row % R) * p.o_rstride;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
         int32_t r[32];
-        __syncwarp();
         tmem_ld32(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c0), r);
         const int64_t col0 = nb * BN + c0;
-        if (row_ok && col0 < p.N) {
-          int v[32];
-          if (p.check) {
+        if (col0 >= p.N) continue;                     // warp-uniform
+        int v[32];
+        if (p.check) {
 #pragma unroll
-            for (int q = 0; q < 32; ++q)
-              v[q] = gemm_epi<true>(r[q], (p.bias && col0 + q < p.N) ? p.bias[col0 + q] : 0, p, lt, lo, hi, bad);
+          for (int q = 0; q < 32; ++q)
+            v[q] = gemm_epi<true>(r[q], (p.bias && col0 + q < p.N) ? p.bias[col0 + q] : 0, p, lt ? p.lut : nullptr,
+                                  lo, hi, bad);
+        } else {
+          // the static int32 proof holds: (acc [+ bias]) * M + 2^(s-1) fits int32, so 32-bit wrap-free math is
+          // exact; a bias arrives pre-folded as bias*M + 2^(s-1) (ANVIL_F_BIAS_RND)
+          int br[32];
+          if (p.bias) {
+            __syncwarp();
+            bslot[lane] = col0 + lane < p.N ? p.bias[col0 + lane] : 0;
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const int4 b4 = reinterpret_cast<const int4 *>(bslot)[q];
+              br[4 * q] = b4.x; br[4 * q + 1] = b4.y; br[4 * q + 2] = b4.z; br[4 * q + 3] = b4.w;
+            }
           } else {
 #pragma unroll
-            for (int q = 0; q < 32; ++q)
-              v[q] = gemm_epi<false>(r[q], (p.bias && col0 + q < p.N) ? p.bias[col0 + q] : 0, p, lt, lo, hi, bad);
+            for (int q = 0; q < 32; ++q) br[q] = rnd;
           }
+#pragma unroll
+          for (int q = 0; q < 32; ++q) {
+            int x = (r[q] * m32 + br[q]) >> sh;
+            x = min(hi, max(lo, x));
+            if (lt) {
+              const int e = x + 128;
+              x = lt[(e >> 2) * 128 + lane * 4 + (e & 3)];
+            }
+            v[q] = x;
+          }
+        }
+        if (row_ok) {
           const int cnt = (int)(p.N - col0 < 32 ? p.N - col0 : 32);
           if (p.o_cstride == 1) {
             store_row32<OB>(orow + col0, v, cnt);

@@ -65,6 +65,8 @@ enum anvil_op_kind {
 #define ANVIL_F_BIAS 8u       /* gemm: int32 bias per column; norm: int8 bias per channel          */
 #define ANVIL_F_CENTER 16u    /* norm: layernorm (mean-centre the row first)                        */
 #define ANVIL_F_SIMT 32u      /* gemm: force the CUDA-core kernel (shapes the TMA path cannot take) */
+#define ANVIL_F_BIAS_RND 64u  /* gemm: the BIAS slot holds bias*M + 2^(s-1) per column (int32); only without
+                                 ANVIL_F_CHECKED, where the int32 proof makes the 32-bit epilogue exact  */
 
 /* One lowered kernel launch. Field meaning per kind (all sizes in elements, offsets in bytes):
  *   GEMM        dims  = {batch, M, N, K}; strides = {a_batch, bt_batch (0: shared weight), out_batch,

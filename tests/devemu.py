@@ -57,9 +57,12 @@ class Emu:
             a = self.get(o.off[0] + b * abs_, M * K, 1).reshape(M, K)
             bt = self.get(o.off[1] + (b * bbs if bbs else 0), N * K, 1).reshape(N, K)
             acc = a @ bt.T
-            if bias is not None:
-                acc = acc + bias
-            v = np.clip((acc * int(o.mult) + _rnd(int(o.shift))) >> int(o.shift), lo, hi)
+            if bias is not None and o.flags & C.F_BIAS_RND:        # folded bias*M + 2^(s-1)
+                v = np.clip((acc * int(o.mult) + bias) >> int(o.shift), lo, hi)
+            else:
+                if bias is not None:
+                    acc = acc + bias
+                v = np.clip((acc * int(o.mult) + _rnd(int(o.shift))) >> int(o.shift), lo, hi)
             if lut is not None:
                 v = lut[v + 128]
             mem, base = self._mem(o.off[2])
