@@ -19,7 +19,7 @@ LIB_PATH = Path(__file__).resolve().parents[1] / "_lib" / "libanvil_cuda.so"
 
 OP_GEMM, OP_LUT, OP_LUT_MUL, OP_ADD_REQUANT, OP_NORM, OP_SOFTMAX, OP_TRANSPOSE, OP_EMBED, OP_ATTENTION, OP_COPY = \
     range(1, 11)
-F_CAUSAL, F_CHECKED, F_LUT, F_BIAS, F_CENTER, F_SIMT, F_BIAS_RND = 1, 2, 4, 8, 16, 32, 64
+F_CAUSAL, F_CHECKED, F_LUT, F_BIAS, F_CENTER, F_SIMT, F_BIAS_RND, F_RESIDUAL = 1, 2, 4, 8, 16, 32, 64, 128
 LOC_CONST = 1 << 63
 LOC_NONE = (1 << 64) - 1
 

@@ -379,7 +379,19 @@ class Lowering:
             a_bs, bt_bs = M * K, N * K
             outs_shape = a.shape[:-1] + (N,)
             per_sample = [(0, 0)]
-        out = self.new_view(out_label, outs_shape, t.dtype)
+        # fused residual add: add_requant(other, y) (either order) where y = this GEMM's result used only there
+        res_add = None
+        if (self.fuse and not self.checked and lut_op is None and id(op) not in self.vt_gemm and batch == 1
+                and len(per_sample) == 1 and id(op.result) not in self.out_ids):
+            us = self.uses.get(id(op.result), [])
+            if len(us) == 1 and isinstance(us[0], g.AddRequantOp) and us[0].a is not us[0].b:
+                add = us[0]
+                other = add.b if add.a is op.result else add.a
+                ov = self.views.get(id(other))
+                if ov is not None and not ov.const and ov.contiguous and ov.shape == tuple(outs_shape):
+                    res_add = (add, ov, add.a is op.result)
+        odtype = t.dtype if res_add is None else g.qt(res_add[0].result).dtype
+        out = self.new_view(out_label if res_add is None else (res_add[0].sym_str or out_label), outs_shape, odtype)
         ostrides = [Mt * N, N, 0, 0, 1]
         if id(op) in self.vt_gemm and batch == 1 and len(per_sample) == 1 and lut_slot is None:
             # head-major transposed output for a fused attention's V: element (b, t, c) at b*C*T + c*T + t
@@ -389,18 +401,32 @@ class Lowering:
             self.fused.append(f"{label}:vT_epilogue")
         if self.gemm_mode == "simt" or (self.gemm_mode == "auto" and Mt * N * K * batch < SIMT_MAX_WORK):
             flags |= C.F_SIMT
+        extra, res_slot = {}, None
+        if res_add is not None:
+            add, ov, y_is_a = res_add
+            flags |= C.F_RESIDUAL
+            res_slot = self.act_slot(ov)
+            reads = reads + [ov.root]
+            extra = {"in_bytes": ISZ[t.dtype], "in2_bytes": ISZ[ov.dtype], "shift2": add.s,
+                     "ma": add.Mb if y_is_a else add.Ma, "mb": add.Ma if y_is_a else add.Mb}
+            out_label = add.sym_str or out_label
         for s_a, _ in per_sample:
             a_elem = s_a * batch * M * K if len(per_sample) > 1 else 0
             o_elem = s_a * batch * M * N if len(per_sample) > 1 else 0
             slots = [self.act_slot(a, a_elem), bt_slot if bt_slot is not None else self.act_slot(bt),
-                     self.act_slot(out, o_elem), lut_slot, bias_slot]
+                     self.act_slot(out, o_elem), lut_slot, bias_slot, res_slot]
             self.emit(C.OP_GEMM, slots,
                       {"dims": [batch, Mt, N, K], "strides": [a_bs, bt_bs] + ostrides[:2] + ostrides[2:],
                        "mult": op.M, "shift": op.s,
-                       "out_bytes": ISZ[t.dtype], "flags": flags}, out_label, reads, [out.root],
+                       "out_bytes": ISZ[odtype], "flags": flags, **extra}, out_label, reads, [out.root],
                       {"ops": 2 * batch * Mt * N * K, "bytes": batch * Mt * K + N * K * (batch if bt_bs else 1)
-                       + batch * Mt * N * ISZ[t.dtype]})
-        self.views[id(out_val)] = out
+                       + batch * Mt * N * ISZ[odtype]})
+        if res_add is not None:
+            self.views[id(res_add[0].result)] = out
+            self.skip.add(self.func.ops.index(res_add[0]))
+            self.fused.append(f"{label}+{res_add[0].sym_str}:residual_epilogue")
+        else:
+            self.views[id(out_val)] = out
         if lut_op is not None:
             self.skip.add(self.func.ops.index(lut_op))
             self.fused.append(f"{label}+{out_label}:lut_epilogue")

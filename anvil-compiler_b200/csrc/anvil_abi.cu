@@ -266,6 +266,19 @@ static int prepare_gemm(anvil_model *m, Launch &L) {
   memset(&p, 0, sizeof p);
   p.batch = batch; p.M = M; p.N = N; p.K = K;
   p.a_bstride = a_bs; p.bt_bstride = bt_bs; p.o_bstride = o_bs; p.o_rstride = o_rs;
+  if (op.flags & ANVIL_F_RESIDUAL) {
+    if ((op.flags & ANVIL_F_CHECKED) || (op.flags & ANVIL_F_LUT) || batch != 1 || o_rs != N || o_cs != 1 ||
+        op.strides[4] != 0 || (op.in_bytes != 1 && op.in_bytes != 2) || (op.in2_bytes != 1 && op.in2_bytes != 2) ||
+        op.shift2 < 0 || op.shift2 > 31)
+      return fail(ANVIL_E_BAD_ARG, "op %d: bad fused residual gemm", op.op_index);
+    if ((rc = resolve(m, op, 5, (uint64_t)M * N * op.in2_bytes, &L.ptr[5]))) return rc;
+    p.res = L.ptr[5];
+    p.res_bytes = op.in2_bytes;
+    p.y_bytes = op.in_bytes;
+    p.shift2 = (int)op.shift2;
+    p.ma = (int)op.ma;
+    p.mb = (int)op.mb;
+  }
   p.o_group = op.strides[4];
   p.o_gstride = op.strides[5];
   p.o_cstride = op.strides[6] ? op.strides[6] : 1;
@@ -506,6 +519,23 @@ static int launch_op(anvil_model *m, Launch &L) {
       break;
     }
     case ANVIL_OP_NORM: {
+      const int dd = (int)op.dims[1];
+      if (!chk && op.in_bytes == 1 && dd % 16 == 0 && dd <= 2048 && aligned16(L.ptr[0]) &&
+          aligned16(L.ptr[1]) && aligned16(L.ptr[3]) && (!L.ptr[4] || aligned16(L.ptr[4]))) {
+        const int nv = (dd / 16 + 31) / 32;
+        const int g = grid_for(m, op.dims[0], 8, 16);
+        const int8_t *bias = (op.flags & ANVIL_F_BIAS) ? (const int8_t *)L.ptr[4] : nullptr;
+#define NV_LAUNCH(NV)                                                                                             \
+  norm_vec_kernel<NV><<<g, 256, 0, st>>>((const int8_t *)L.ptr[0], (const int8_t *)L.ptr[1],                      \
+                                         (const int32_t *)L.ptr[2], bias, (int8_t *)L.ptr[3], op.dims[0], dd,      \
+                                         (int)op.dims[2], (int)op.mult, (int)op.shift, (int)op.ss_shift,          \
+                                         (int)op.ss_init, (op.flags & ANVIL_F_CENTER) ? 1 : 0)
+        if (nv <= 1) NV_LAUNCH(1);
+        else if (nv == 2) NV_LAUNCH(2);
+        else NV_LAUNCH(4);
+#undef NV_LAUNCH
+        break;
+      }
       auto k = op.in_bytes == 1 ? (chk ? norm_kernel<1, true> : norm_kernel<1, false>)
                                 : (chk ? norm_kernel<2, true> : norm_kernel<2, false>);
       k<<<grid_for(m, d[0], 8), 256, 0, st>>>(L.ptr[0], (const int8_t *)L.ptr[1], (const int32_t *)L.ptr[2],

@@ -13,7 +13,7 @@
 //              TMEM, requant to int8, track the partial row max, store into the P slab j in shared memory (the
 //              128-byte-swizzled K-major layout the P @ V MMA reads); combine the row max across the four parts,
 //              then the two exact softmax passes (partial sums of exp_lut combined the same way, then
-//              (e*one + S/2) / S by a float reciprocal with an integer correction step), then O from TMEM ->
+//              (e*one + S/2) / S as a multiply by a per-row invariant-divisor magic number), then O from TMEM ->
 //              requant -> global
 // The whole score row (up to 1024 keys, int8) stays in shared memory, so the row max and row sum are exact before
 // any probability is formed, as the reference's three-stage loop nest requires; an online (rescaled) softmax
@@ -218,13 +218,23 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(sb * 128 + part * 32), acc);
       uint32_t w[8];
       const int cbase = j * 128 + part * 32;
+      // the static int32 proof holds on this path: acc*M1 + 2^(s1-1) fits int32
+      if (cbase + 32 <= kept) {             // every column of this part is kept: no mask test
 #pragma unroll
-      for (int q = 0; q < 32; ++q) {
-        // the static int32 proof holds on this path: acc*M1 + 2^(s1-1) fits int32
-        const int v = min(127, max(-128, (acc[q] * m1 + rnd1) >> p.s1));
-        if (cbase + q < kept) mx = max(mx, v);
-        if ((q & 3) == 0) w[q >> 2] = 0;
-        w[q >> 2] |= ((uint32_t)(uint8_t)v) << (8 * (q & 3));
+        for (int q = 0; q < 32; ++q) {
+          const int v = min(127, max(-128, (acc[q] * m1 + rnd1) >> p.s1));
+          mx = max(mx, v);
+          if ((q & 3) == 0) w[q >> 2] = 0;
+          w[q >> 2] |= ((uint32_t)(uint8_t)v) << (8 * (q & 3));
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          const int v = min(127, max(-128, (acc[q] * m1 + rnd1) >> p.s1));
+          if (cbase + q < kept) mx = max(mx, v);
+          if ((q & 3) == 0) w[q >> 2] = 0;
+          w[q >> 2] |= ((uint32_t)(uint8_t)v) << (8 * (q & 3));
+        }
       }
       uint8_t *slab = pbuf + j * Cfg::P_SLAB;
       *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part)) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -238,6 +248,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     mx = max(max(red[r], red[128 + r]), max(red[256 + r], red[384 + r]));
     asm volatile("bar.sync 1, 512;" ::: "memory");
     const int base_idx = 255 - mx;
+    const int32_t *lutc = lut + base_idx * Cfg::LUT_COPIES + lcopy;     // lutc[x * COPIES] = lut[x - max + 255]
     // pass A: partial S = sum over this part's kept columns of lut[x - max + 255]
     int tot = 0;
     for (int j = 0; j < nkv && ok; ++j) {
@@ -248,10 +259,18 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         if (c0 < kept) {
           const uint4 v4 = *reinterpret_cast<const uint4 *>(slab + pslab_off(r, 2 * part + hh));
           const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
+          if (c0 + 16 <= kept) {
 #pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            const int x = (int)(int8_t)(wv[q >> 2] >> (8 * (q & 3)));
-            if (c0 + q < kept) tot += lut[(x + base_idx) * Cfg::LUT_COPIES + lcopy];
+            for (int q = 0; q < 16; ++q) {
+              const int x = (int)(int8_t)(wv[q >> 2] >> (8 * (q & 3)));
+              tot += lutc[x * Cfg::LUT_COPIES];
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              const int x = (int)(int8_t)(wv[q >> 2] >> (8 * (q & 3)));
+              if (c0 + q < kept) tot += lutc[x * Cfg::LUT_COPIES];
+            }
           }
         }
       }
@@ -259,10 +278,17 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     red[part * 128 + r] = tot;
     asm volatile("bar.sync 1, 512;" ::: "memory");
     tot = red[r] + red[128 + r] + red[256 + r] + red[384 + r];
-    // pass B: p = floor((e*one + S/2) / S), masked entries 0; float reciprocal + one exact correction step
+    // pass B: p = floor((e*one + S/2) / S), masked entries 0. The division is a multiply by a per-row magic
+    // number (Granlund & Montgomery, "Division by invariant integers using multiplication", 1994): with
+    // l = ceil(log2 S), k = 31 + l and m = ceil(2^k / S) (m <= 2^32), floor(n m / 2^k) = floor(n / S) for every
+    // 0 <= n < 2^31, because m S - 2^k < S <= 2^l makes the error term n (m S - 2^k) / (S 2^k) < 1 / S.
+    // With m < 2^32 this is a 32 x 32 -> high 32 multiply and a shift by l - 1; S = 1 (l = 0) passes n through.
     const int S = tot > 0 ? tot : 1;
     const int half = tot >> 1;
-    const float rS = 1.0f / (float)S;
+    const int lg = S > 1 ? 32 - __clz(S - 1) : 0;
+    const unsigned magic = (unsigned)(((1ull << (31 + lg)) + (unsigned long long)(S - 1)) / (unsigned long long)S);
+    const int msh = lg > 0 ? lg - 1 : 0;
+    const bool s_is_one = S == 1;
     const int one = p.one;
     for (int j = 0; j < nkv && ok; ++j) {
       uint8_t *slab = pbuf + j * Cfg::P_SLAB;
@@ -273,19 +299,24 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         uint4 v4 = *reinterpret_cast<const uint4 *>(slab + off);
         const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
         uint32_t ov[4] = {0, 0, 0, 0};
-        if (c0 < kept) {
+        if (c0 + 16 <= kept) {
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
             const int x = (int)(int8_t)(wv[q >> 2] >> (8 * (q & 3)));
-            int pq = 0;
+            const unsigned num = (unsigned)(lutc[x * Cfg::LUT_COPIES] * one + half);
+            const unsigned pq = s_is_one ? num : (__umulhi(num, magic) >> msh);
+            ov[q >> 2] |= (pq & 0xffu) << (8 * (q & 3));
+          }
+        } else if (c0 < kept) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const int x = (int)(int8_t)(wv[q >> 2] >> (8 * (q & 3)));
+            unsigned pq = 0;
             if (c0 + q < kept) {
-              const int num = lut[(x + base_idx) * Cfg::LUT_COPIES + lcopy] * one + half;
-              int qq = __float2int_rz((float)num * rS);
-              const int rem = num - qq * S;
-              qq += (rem >= S) - (rem < 0);
-              pq = qq;
+              const unsigned num = (unsigned)(lutc[x * Cfg::LUT_COPIES] * one + half);
+              pq = s_is_one ? num : (__umulhi(num, magic) >> msh);
             }
-            ov[q >> 2] |= ((uint32_t)(uint8_t)pq) << (8 * (q & 3));
+            ov[q >> 2] |= (pq & 0xffu) << (8 * (q & 3));
           }
         }
         *reinterpret_cast<uint4 *>(slab + off) = make_uint4(ov[0], ov[1], ov[2], ov[3]);

@@ -34,7 +34,20 @@ struct GemmParams {
   uint32_t *flags;
   int op_index;
   int64_t m_tiles, n_tiles, tiles;     // tc path tiling
+  // fused residual add (unchecked only): out = clamp((res*ma + y*mb + 2^(s2-1)) >> s2) where y is the requant
+  // result clamped to y_bytes' range and res is (M, N) row-major with res_bytes per element
+  const void *res;
+  int res_bytes, y_bytes, shift2;
+  int ma, mb;
 };
+
+// y -> the fused residual add's result (32-bit exact under the static int32 proof)
+template <int OB>
+__device__ __forceinline__ int residual_add(int y, int rv, const GemmParams &p) {
+  constexpr int lo = OB == 1 ? -128 : -32768, hi = OB == 1 ? 127 : 32767;
+  const int rnd2 = p.shift2 ? 1 << (p.shift2 - 1) : 0;
+  return min(hi, max(lo, (rv * p.ma + y * p.mb + rnd2) >> p.shift2));
+}
 
 // One output element from its int32 accumulator (shared by both kernels).
 template <bool CHECK>
@@ -102,11 +115,19 @@ __global__ void __launch_bounds__(256) qgemm_simt_kernel(GemmParams p) {
       int64_t gj = j0 + tx + 16 * r;
       if (gj >= p.N) continue;
       int v;
+      const int ylo = p.res ? (p.y_bytes == 1 ? -128 : -32768) : lo, yhi = p.res ? (p.y_bytes == 1 ? 127 : 32767) : hi;
       if (CHECK || !p.bias) {
-        v = gemm_epi<CHECK>(acc[q][r], p.bias ? p.bias[gj] : 0, p, lt, lo, hi, bad);
+        v = gemm_epi<CHECK>(acc[q][r], p.bias ? p.bias[gj] : 0, p, lt, ylo, yhi, bad);
       } else {                  // bias folded as bias*M + 2^(s-1) (ANVIL_F_BIAS_RND)
-        v = clampi(((long long)acc[q][r] * p.mult + p.bias[gj]) >> p.shift, lo, hi);
+        v = clampi(((long long)acc[q][r] * p.mult + p.bias[gj]) >> p.shift, ylo, yhi);
         if (lt) v = lt[v + 128];
+      }
+      if (p.res) {
+        const int64_t ri = gi * p.N + gj;
+        const int rv = p.res_bytes == 1 ? (int)reinterpret_cast<const int8_t *>(p.res)[ri]
+                                        : (int)reinterpret_cast<const int16_t *>(p.res)[ri];
+        const int rnd2 = p.shift2 ? 1 << (p.shift2 - 1) : 0;
+        v = min(hi, max(lo, (rv * p.ma + v * p.mb + rnd2) >> p.shift2));
       }
       const int64_t R = p.o_group ? p.o_group : p.M;
       int64_t o = b * p.o_bstride + (gi / R) * p.o_gstride + (gi % R) * p.o_rstride + gj * p.o_cstride;
@@ -140,6 +161,37 @@ struct TcCfg {
   static constexpr int BST_OFF = LUT_OFF + 32 * 256;
   static constexpr int SMEM_BYTES = BST_OFF + TC_EPI_WARPS * 128 + 1024;   // + 1 KB slack to align the ring
 };
+
+// Load 32 consecutive int8 / int16 values of a row (vector loads when the chunk is whole and aligned).
+__device__ __forceinline__ void load_row32(const void *base, int bytes, int64_t elem, int count, int (&rv)[32]) {
+  if (bytes == 1) {
+    const int8_t *src = reinterpret_cast<const int8_t *>(base) + elem;
+    if (count == 32 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+      const uint4 a = reinterpret_cast<const uint4 *>(src)[0], b = reinterpret_cast<const uint4 *>(src)[1];
+      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int q = 0; q < 32; ++q) rv[q] = (int)(int8_t)(w[q >> 2] >> (8 * (q & 3)));
+    } else {
+#pragma unroll
+      for (int q = 0; q < 32; ++q) rv[q] = q < count ? (int)src[q] : 0;
+    }
+  } else {
+    const int16_t *src = reinterpret_cast<const int16_t *>(base) + elem;
+    if (count == 32 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+      uint32_t w[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 a = reinterpret_cast<const uint4 *>(src)[q];
+        w[4 * q] = a.x; w[4 * q + 1] = a.y; w[4 * q + 2] = a.z; w[4 * q + 3] = a.w;
+      }
+#pragma unroll
+      for (int q = 0; q < 32; ++q) rv[q] = (int)(int16_t)(w[q >> 1] >> (16 * (q & 1)));
+    } else {
+#pragma unroll
+      for (int q = 0; q < 32; ++q) rv[q] = q < count ? (int)src[q] : 0;
+    }
+  }
+}
 
 // Store 32 consecutive results of one output row: 16-byte vector stores when the whole chunk is in range and
 // aligned, element stores otherwise.
@@ -323,15 +375,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
             for (int q = 0; q < 32; ++q) br[q] = rnd;
           }
+          if (!p.res) {
 #pragma unroll
-          for (int q = 0; q < 32; ++q) {
-            int x = (r[q] * m32 + br[q]) >> sh;
-            x = min(hi, max(lo, x));
-            if (lt) {
-              const int e = x + 128;
-              x = lt[(e >> 2) * 128 + lane * 4 + (e & 3)];
+            for (int q = 0; q < 32; ++q) {
+              int x = (r[q] * m32 + br[q]) >> sh;
+              x = min(hi, max(lo, x));
+              if (lt) {
+                const int e = x + 128;
+                x = lt[(e >> 2) * 128 + lane * 4 + (e & 3)];
+              }
+              v[q] = x;
             }
-            v[q] = x;
+          } else {          // fused residual add: y clamped to its own dtype, then res*Ma + y*Mb requantised
+            const int ylo = p.y_bytes == 1 ? -128 : -32768, yhi = p.y_bytes == 1 ? 127 : 32767;
+            int rv[32];
+            const int cnt = (int)(p.N - col0 < 32 ? p.N - col0 : 32);
+            if (row_ok) load_row32(p.res, p.res_bytes, row * p.N + col0, cnt, rv);
+#pragma unroll
+            for (int q = 0; q < 32; ++q) {
+              const int y = min(yhi, max(ylo, (r[q] * m32 + br[q]) >> sh));
+              v[q] = residual_add<OB>(y, row_ok ? rv[q] : 0, p);
+            }
           }
         }
         if (row_ok) {

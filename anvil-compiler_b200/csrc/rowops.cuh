@@ -174,6 +174,92 @@ __global__ void norm_kernel(const void *__restrict__ x_, const int8_t *__restric
   if (__any_sync(0xffffffffu, badidx) && badidx) raise_flag(flags, FLAG_INDEX, op_index);
 }
 
+// Vectorised form for int8 rows with d % 16 == 0 and d <= 512 * NV, when the static int32 proof holds (no
+// device checks): one warp per row, the row, the weights and the bias held in registers as 16-byte vectors
+// (NV per lane), one read and one write of the row, 32-bit arithmetic (every intermediate is proven to fit).
+__device__ __forceinline__ int sext8(uint32_t w, int q) { return (int)(int8_t)(w >> (8 * q)); }
+
+template <int NV>
+__global__ void __launch_bounds__(256) norm_vec_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w,
+                                                       const int32_t *__restrict__ lut,
+                                                       const int8_t *__restrict__ bias, int8_t *__restrict__ out,
+                                                       int64_t rows, int d, int n, int m, int s, int c, int e,
+                                                       int center) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = d >> 4;
+  uint4 wv[NV], bv[NV];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int iv = lane + 32 * v;
+    wv[v] = iv < nvec ? reinterpret_cast<const uint4 *>(w)[iv] : make_uint4(0, 0, 0, 0);
+    bv[v] = (bias && iv < nvec) ? reinterpret_cast<const uint4 *>(bias)[iv] : make_uint4(0, 0, 0, 0);
+  }
+  const int rc = c ? 1 << (c - 1) : 0;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = warp; row < rows; row += nwarps) {
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * d);
+    uint4 xv[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int iv = lane + 32 * v;
+      xv[v] = iv < nvec ? xr[iv] : make_uint4(0, 0, 0, 0);
+    }
+    int mean = 0;
+    if (center) {
+      int sum = 0;
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const uint32_t ws[4] = {xv[v].x, xv[v].y, xv[v].z, xv[v].w};
+#pragma unroll
+        for (int q = 0; q < 16; ++q) sum += sext8(ws[q >> 2], q & 3);
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      const int num = sum + d / 2;                        // floor division by d > 0
+      mean = num >= 0 ? num / d : -((-num + d - 1) / d);
+    }
+    int ss = 0;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      if (lane + 32 * v >= nvec) continue;
+      const uint32_t ws[4] = {xv[v].x, xv[v].y, xv[v].z, xv[v].w};
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const int xc = sext8(ws[q >> 2], q & 3) - mean;
+        ss += (xc * xc + rc) >> c;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    ss += e;
+    int idx = ss, k = 0;
+    while (idx >= n) { idx >>= 2; ++k; }
+    const int r = lut[idx];
+    const int sh = s + k;
+    const int rnd = sh ? 1 << (sh - 1) : 0;
+    uint4 *orow = reinterpret_cast<uint4 *>(out + row * d);
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int iv = lane + 32 * v;
+      if (iv >= nvec) continue;
+      const uint32_t ws[4] = {xv[v].x, xv[v].y, xv[v].z, xv[v].w};
+      const uint32_t ww[4] = {wv[v].x, wv[v].y, wv[v].z, wv[v].w};
+      const uint32_t bb[4] = {bv[v].x, bv[v].y, bv[v].z, bv[v].w};
+      uint32_t o4[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const int xc = sext8(ws[q >> 2], q & 3) - mean;
+        int y = ((xc * sext8(ww[q >> 2], q & 3) * r) * m + rnd) >> sh;
+        y += sext8(bb[q >> 2], q & 3);
+        y = min(127, max(-128, y));
+        o4[q >> 2] |= ((uint32_t)(uint8_t)y) << (8 * (q & 3));
+      }
+      orow[iv] = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ softmax
 // softmax_lut (anvil/lower/graph_to_tensor.py:352-398): one warp per row of (batch, T1, T2); kept j <= i when
 // causal; m = max(-128, x_j); e_j = lut[x_j - m + 255]; S = sum e_j; p_j = (e_j*one + S/2) / S (floor).

@@ -67,13 +67,16 @@ enum anvil_op_kind {
 #define ANVIL_F_SIMT 32u      /* gemm: force the CUDA-core kernel (shapes the TMA path cannot take) */
 #define ANVIL_F_BIAS_RND 64u  /* gemm: the BIAS slot holds bias*M + 2^(s-1) per column (int32); only without
                                  ANVIL_F_CHECKED, where the int32 proof makes the 32-bit epilogue exact  */
+#define ANVIL_F_RESIDUAL 128u /* gemm: fused add_requant with off[5] = RES ((M, N) row-major, in2_bytes):
+                                 out = clamp((res*ma + y*mb + 2^(shift2-1)) >> shift2), y the requant result
+                                 clamped to in_bytes' range; unchecked, unbatched, row-major output only     */
 
 /* One lowered kernel launch. Field meaning per kind (all sizes in elements, offsets in bytes):
  *   GEMM        dims  = {batch, M, N, K}; strides = {a_batch, bt_batch (0: shared weight), out_batch,
  *                       out_row, out_group_rows (0: M), out_group, out_col (0: 1)}: element (b, row, col) goes to
  *                       b*out_batch + (row / R)*out_group + (row % R)*out_row + col*out_col;
  *                       off = {A (batch, M, K) int8, BT (batch|1, N, K) int8, OUT, LUT (256 i8), BIAS (N i32)};
- *                       mult = M, shift = s; out_bytes = 1 (i8) or 2 (i16)
+ *                       mult = M, shift = s; out_bytes = 1 (i8) or 2 (i16); ANVIL_F_RESIDUAL adds off[5]
  *   LUT         dims  = {n}; off = {X, TABLE, OUT}
  *   LUT_MUL     dims  = {n}; off = {X, Y, TABLE, OUT}; mult, shift
  *   ADD_REQUANT dims  = {n}; off = {A, B, OUT}; in_bytes = a bytes, in2_bytes = b bytes, out_bytes;

@@ -65,6 +65,13 @@ class Emu:
                 v = np.clip((acc * int(o.mult) + _rnd(int(o.shift))) >> int(o.shift), lo, hi)
             if lut is not None:
                 v = lut[v + 128]
+            if o.flags & C.F_RESIDUAL:                                  # y clamped to its dtype, then the add
+                y = np.clip(np.clip((acc * int(o.mult) + (bias if bias is not None and o.flags & C.F_BIAS_RND
+                                                          else _rnd(int(o.shift)))) >> int(o.shift),
+                                    *RANGE[o.in_bytes]), *RANGE[o.in_bytes])
+                res = self.get(o.off[5], M * N, o.in2_bytes).reshape(M, N)
+                s2 = int(o.shift2)
+                v = np.clip((res * int(o.ma) + y * int(o.mb) + _rnd(s2)) >> s2, lo, hi)
             mem, base = self._mem(o.off[2])
             idx = (b * obs + (np.arange(M)[:, None] // grp) * gst + (np.arange(M)[:, None] % grp) * ors
                    + np.arange(N)[None, :] * cst)

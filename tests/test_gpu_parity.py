@@ -194,3 +194,11 @@ def test_c3_block_fused_matches_oracle():
     res = cm.run(xq, "cuda", quantized=True)
     assert any("attention" in f for f in res.job.fused)
     _check(res.ints, want.values, cm.outputs)
+
+
+@pytest.mark.parametrize("seed", range(40, 56))
+def test_random_graphs_unchecked_fused(seed):
+    m, c, x, want = random_case(seed, batch=3, big=seed % 2 == 0)
+    cm = anvil.compile(m, consts=c, prove=False, params=CudaParams(checked=False))
+    res = cm.run([x[s] for s in cm.inputs], "cuda", quantized=True)
+    _check(res.ints, want.values, cm.outputs)

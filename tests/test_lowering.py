@@ -72,3 +72,12 @@ def test_plan_reuses_and_never_overlaps_live_buffers():
         assert not memplan.check_disjoint(plan.bufs.values(), plan.addresses)
         assert all(a % memplan.ALIGN == 0 for a in plan.addresses.values())
     assert cm.program(4).plan.arena <= cm.program(4).plan.unshared
+
+
+@pytest.mark.parametrize("seed", range(30, 50))
+def test_random_graph_unchecked_fusions(seed):
+    """With checked=False every fusion applies; on inputs the oracle accepted no intermediate overflowed, so the
+    32-bit epilogues are exact and the launch list must still match."""
+    m, c, x, want = random_case(seed, batch=2)
+    cm = anvil.compile(m, consts=c, prove=False, params=CudaParams(checked=False))
+    _check(run_program(cm, x), want.values, cm.outputs)
