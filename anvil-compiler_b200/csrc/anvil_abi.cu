@@ -192,12 +192,11 @@ extern "C" int anvil_model_create(int device, const void *consts, uint64_t const
     int r = 0;
     r |= set_smem(attn_kernel<64>, AttnCfg<64>::SMEM_BYTES);
     r |= set_smem(attn_kernel<128>, AttnCfg<128>::SMEM_BYTES);
-    r |= set_smem(qgemm_tc_kernel<64, 1>, TcCfg<64>::SMEM_BYTES);
-    r |= set_smem(qgemm_tc_kernel<64, 2>, TcCfg<64>::SMEM_BYTES);
-    r |= set_smem(qgemm_tc_kernel<128, 1>, TcCfg<128>::SMEM_BYTES);
-    r |= set_smem(qgemm_tc_kernel<128, 2>, TcCfg<128>::SMEM_BYTES);
-    r |= set_smem(qgemm_tc_kernel<256, 1>, TcCfg<256>::SMEM_BYTES);
-    r |= set_smem(qgemm_tc_kernel<256, 2>, TcCfg<256>::SMEM_BYTES);
+#define TC_ATTR(BN, OB)                                                        \
+  r |= set_smem(qgemm_tc_kernel<BN, OB, false>, TcCfg<BN>::SMEM_BYTES);      \
+  r |= set_smem(qgemm_tc_kernel<BN, OB, true>, TcCfg<BN>::SMEM_BYTES);
+    TC_ATTR(64, 1) TC_ATTR(64, 2) TC_ATTR(128, 1) TC_ATTR(128, 2) TC_ATTR(256, 1) TC_ATTR(256, 2)
+#undef TC_ATTR
     if (r) return cleanup(ANVIL_E_CUDA);
     attrs[device] = true;
   }
@@ -479,7 +478,11 @@ static int launch_op(anvil_model *m, Launch &L) {
       GemmParams &p = L.gp;
       if (L.tc) {
         const int grid = (int)std::min<int64_t>(p.tiles, m->sms);
-#define TC_LAUNCH(BN, OB) qgemm_tc_kernel<BN, OB><<<grid, TC_THREADS, TcCfg<BN>::SMEM_BYTES, st>>>(L.mapA, L.mapB, p)
+#define TC_LAUNCH(BN, OB)                                                                                       \
+  do {                                                                                                          \
+    if (p.res) qgemm_tc_kernel<BN, OB, true><<<grid, TC_THREADS, TcCfg<BN>::SMEM_BYTES, st>>>(L.mapA, L.mapB, p);  \
+    else qgemm_tc_kernel<BN, OB, false><<<grid, TC_THREADS, TcCfg<BN>::SMEM_BYTES, st>>>(L.mapA, L.mapB, p);       \
+  } while (0)
         if (L.bn == 64) { if (op.out_bytes == 1) TC_LAUNCH(64, 1); else TC_LAUNCH(64, 2); }
         else if (L.bn == 128) { if (op.out_bytes == 1) TC_LAUNCH(128, 1); else TC_LAUNCH(128, 2); }
         else { if (op.out_bytes == 1) TC_LAUNCH(256, 1); else TC_LAUNCH(256, 2); }

@@ -218,32 +218,30 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(sb * 128 + part * 32), acc);
       uint32_t w[8];
       const int cbase = j * 128 + part * 32;
-      // the static int32 proof holds on this path: acc*M1 + 2^(s1-1) fits int32
+      // the static int32 proof holds on this path: acc*M1 + 2^(s1-1) fits int32. The row max is taken over the
+      // unclamped values (clamping is monotone, so max of clamped = clamp of max) and the clamp happens in the
+      // saturating pack.
+      int v[32];
+#pragma unroll
+      for (int q = 0; q < 32; ++q) v[q] = (acc[q] * m1 + rnd1) >> p.s1;
       if (cbase + 32 <= kept) {             // every column of this part is kept: no mask test
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const int v = min(127, max(-128, (acc[q] * m1 + rnd1) >> p.s1));
-          mx = max(mx, v);
-          if ((q & 3) == 0) w[q >> 2] = 0;
-          w[q >> 2] |= ((uint32_t)(uint8_t)v) << (8 * (q & 3));
-        }
+        for (int q = 0; q < 32; ++q) mx = max(mx, v[q]);
       } else {
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const int v = min(127, max(-128, (acc[q] * m1 + rnd1) >> p.s1));
-          if (cbase + q < kept) mx = max(mx, v);
-          if ((q & 3) == 0) w[q >> 2] = 0;
-          w[q >> 2] |= ((uint32_t)(uint8_t)v) << (8 * (q & 3));
-        }
+        for (int q = 0; q < 32; ++q)
+          if (cbase + q < kept) mx = max(mx, v[q]);
       }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
       uint8_t *slab = pbuf + j * Cfg::P_SLAB;
       *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part)) = make_uint4(w[0], w[1], w[2], w[3]);
       *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
       tc_fence_before();
       mbar_arrive(&sempty[sb]);
     }
-    // row max over the 4 parts
-    red[part * 128 + r] = mx;
+    // row max over the 4 parts (clamped: the raw scores were tracked)
+    red[part * 128 + r] = min(127, mx);
     asm volatile("bar.sync 1, 512;" ::: "memory");
     mx = max(max(red[r], red[128 + r]), max(red[256 + r], red[384 + r]));
     asm volatile("bar.sync 1, 512;" ::: "memory");
@@ -262,14 +260,12 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           if (c0 + 16 <= kept) {
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
-              const int x = (int)(int8_t)(wv[q >> 2] >> (8 * (q & 3)));
-              tot += lutc[x * Cfg::LUT_COPIES];
+              tot += lutc[sbyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES];
             }
           } else {
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
-              const int x = (int)(int8_t)(wv[q >> 2] >> (8 * (q & 3)));
-              if (c0 + q < kept) tot += lutc[x * Cfg::LUT_COPIES];
+              if (c0 + q < kept) tot += lutc[sbyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES];
             }
           }
         }
@@ -300,13 +296,14 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
         uint32_t ov[4] = {0, 0, 0, 0};
         if (c0 + 16 <= kept) {
+          int pv[16];
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            const int x = (int)(int8_t)(wv[q >> 2] >> (8 * (q & 3)));
-            const unsigned num = (unsigned)(lutc[x * Cfg::LUT_COPIES] * one + half);
-            const unsigned pq = s_is_one ? num : (__umulhi(num, magic) >> msh);
-            ov[q >> 2] |= (pq & 0xffu) << (8 * (q & 3));
+            const unsigned num = (unsigned)(lutc[sbyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES] * one + half);
+            pv[q] = (int)(s_is_one ? num : (__umulhi(num, magic) >> msh));
           }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) ov[q] = pack4_sat_s8(pv[4 * q], pv[4 * q + 1], pv[4 * q + 2], pv[4 * q + 3]);
         } else if (c0 < kept) {
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
@@ -331,12 +328,11 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       int32_t acc[32];
       tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(256 + part * 32), acc);
       uint32_t w[8];
+      int v[32];
 #pragma unroll
-      for (int q = 0; q < 32; ++q) {
-        const int v = clampi(((long long)acc[q] * p.m2 + rnd2) >> p.s2, -128, 127);
-        if ((q & 3) == 0) w[q >> 2] = 0;
-        w[q >> 2] |= ((uint32_t)(uint8_t)v) << (8 * (q & 3));
-      }
+      for (int q = 0; q < 32; ++q) v[q] = (int)clampi(((long long)acc[q] * p.m2 + rnd2) >> p.s2, -128, 127);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
       if (row < p.T1) {
         int8_t *orow = p.out + (int64_t)b * p.o_bs + (int64_t)row * p.o_rs + (int64_t)h * HD + part * 32;
         uint4 *d4 = reinterpret_cast<uint4 *>(orow);

@@ -53,6 +53,18 @@ struct IntOf<4> { using T = int32_t; };
 
 }  // namespace anvil
 
+// Saturate four int32 values to int8 and pack them little-endian (a0 in byte 0) with two cvt.pack.sat ops:
+// cvt.pack.sat.s8.s32.b32 d, a, b, c puts sat8(b) in d[7:0], sat8(a) in d[15:8] and c[15:0] in d[31:16].
+__device__ __forceinline__ uint32_t pack4_sat_s8(int a0, int a1, int a2, int a3) {
+  uint32_t hi, d;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(a3), "r"(a2));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a1), "r"(a0), "r"(hi));
+  return d;
+}
+
+// Signed byte q (0..3) of w, sign-extended: always in [-128, 127].
+__device__ __forceinline__ int sbyte(uint32_t w, int q) { return (int)(int8_t)(w >> (8 * q)); }
+
 // ------------------------------------------------------------------------------------------------- PTX: misc
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {

@@ -198,12 +198,10 @@ __device__ __forceinline__ void load_row32(const void *base, int bytes, int64_t 
 template <int OB>
 __device__ __forceinline__ void store_row32(typename IntOf<OB>::T *dst, const int (&v)[32], int count) {
   if (count == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-    if (OB == 1) {
+    if (OB == 1) {                      // saturating pack: values may arrive unclamped
       uint32_t w[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        w[q] = (uint32_t)(uint8_t)v[4 * q] | ((uint32_t)(uint8_t)v[4 * q + 1] << 8) |
-               ((uint32_t)(uint8_t)v[4 * q + 2] << 16) | ((uint32_t)(uint8_t)v[4 * q + 3] << 24);
+      for (int q = 0; q < 8; ++q) w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
       uint4 *d4 = reinterpret_cast<uint4 *>(dst);
       d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
       d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
@@ -218,11 +216,11 @@ __device__ __forceinline__ void store_row32(typename IntOf<OB>::T *dst, const in
   } else {
 #pragma unroll
     for (int q = 0; q < 32; ++q)
-      if (q < count) dst[q] = (typename IntOf<OB>::T)v[q];
+      if (q < count) dst[q] = (typename IntOf<OB>::T)(OB == 1 ? min(127, max(-128, v[q])) : v[q]);
   }
 }
 
-template <int BN, int OB>
+template <int BN, int OB, bool RES>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const GemmParams p) {
@@ -375,11 +373,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
             for (int q = 0; q < 32; ++q) br[q] = rnd;
           }
-          if (!p.res) {
+          if (!RES) {
 #pragma unroll
             for (int q = 0; q < 32; ++q) {
               int x = (r[q] * m32 + br[q]) >> sh;
-              x = min(hi, max(lo, x));
+              if (OB != 1 || lt) x = min(hi, max(lo, x));      // i8 without a LUT saturates in the pack
               if (lt) {
                 const int e = x + 128;
                 x = lt[(e >> 2) * 128 + lane * 4 + (e & 3)];
@@ -406,7 +404,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             TO *dst = orow + col0 * p.o_cstride;
 #pragma unroll
             for (int q = 0; q < 32; ++q)
-              if (q < cnt) dst[q * p.o_cstride] = (TO)v[q];
+              if (q < cnt) dst[q * p.o_cstride] = (TO)min(hi, max(lo, v[q]));
           }
         }
       }
