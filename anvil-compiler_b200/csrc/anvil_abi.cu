@@ -162,6 +162,8 @@ static int set_smem(K kernel, int bytes) {
   return ANVIL_OK;
 }
 
+static int kernel_attrs(int device);
+
 extern "C" int anvil_model_create(int device, const void *consts, uint64_t const_bytes, anvil_model **out) {
   if (!out) return fail(ANVIL_E_BAD_ARG, "out is NULL");
   *out = nullptr;
@@ -187,8 +189,16 @@ extern "C" int anvil_model_create(int device, const void *consts, uint64_t const
       return cleanup(fail(ANVIL_E_CUDA, "const upload failed"));
   }
   m->const_bytes = const_bytes;
+  if ((rc = kernel_attrs(device))) return cleanup(rc);
+  *out = m;
+  return ANVIL_OK;
+}
+
+// Opt every large-shared-memory kernel in to its dynamic shared memory size on `device` (current), once.
+static int kernel_attrs(int device) {
   static bool attrs[64] = {};     // the attribute is per function and per device
-  if (device < 64 && !attrs[device]) {
+  if (device >= 64) return fail(ANVIL_E_BAD_ARG, "device %d out of range", device);
+  if (!attrs[device]) {
     int r = 0;
     r |= set_smem(attn_kernel<64>, AttnCfg<64>::SMEM_BYTES);
     r |= set_smem(attn_kernel<128>, AttnCfg<128>::SMEM_BYTES);
@@ -197,10 +207,9 @@ extern "C" int anvil_model_create(int device, const void *consts, uint64_t const
   r |= set_smem(qgemm_tc_kernel<BN, OB, true>, TcCfg<BN>::SMEM_BYTES);
     TC_ATTR(64, 1) TC_ATTR(64, 2) TC_ATTR(128, 1) TC_ATTR(128, 2) TC_ATTR(256, 1) TC_ATTR(256, 2)
 #undef TC_ATTR
-    if (r) return cleanup(ANVIL_E_CUDA);
+    if (r) return ANVIL_E_CUDA;
     attrs[device] = true;
   }
-  *out = m;
   return ANVIL_OK;
 }
 
@@ -781,4 +790,86 @@ extern "C" int anvil_gemm_requant(const int8_t *A, const int8_t *BT, int8_t *out
     return check_flags(m, h);
   }
   return ANVIL_OK;
+}
+
+// ------------------------------------------------------------------- standalone GEMM without allocation
+//
+// For callers that must not allocate device memory (an embedding whose host owns every allocation, code running
+// where cudaMalloc is unavailable or forbidden): the same GEMM + requant as anvil_gemm_requant, but the only device
+// memory beyond the caller's A, BT and out is this file-scope array, which holds the kernel's status words
+// (overflow / index / device-wait timeout). Every GPU that loads the library keeps one copy until the process
+// exits. The host reaches the copy of the current device through cudaGetSymbolAddress, once per device.
+
+#define ANVIL_NOALLOC_SCRATCH_WORDS 16            // 64 bytes; the GEMM needs FLAG_WORDS of them
+static __device__ __align__(256) uint32_t g_noalloc_scratch[ANVIL_NOALLOC_SCRATCH_WORDS];
+
+extern "C" int anvil_gemm_requant_noalloc(const int8_t *A, const int8_t *BT, int8_t *out, int64_t M, int64_t N,
+                                          int64_t K, int32_t mult, int32_t shift, uint32_t flags, void *stream) {
+  if (!A || !BT || !out || M < 1 || N < 1 || K < 1 || shift < 0 || shift > 31)
+    return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_gemm_requant_noalloc");
+  if (FLAG_WORDS > ANVIL_NOALLOC_SCRATCH_WORDS)
+    return fail(ANVIL_E_BAD_ARG, "anvil_gemm_requant_noalloc needs %d scratch words, the static array holds %d",
+                (int)FLAG_WORDS, ANVIL_NOALLOC_SCRATCH_WORDS);
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  if (dev >= 64) return fail(ANVIL_E_BAD_ARG, "device %d out of range", dev);
+  // set-up, once per device, with that device current: the array's device address, the SM count and the kernels'
+  // shared-memory opt-in. None of it allocates.
+  static uint32_t *scratch_ptr[64] = {};
+  static int sm_count[64] = {};
+  if (!scratch_ptr[dev]) {
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, dev));
+    if (prop.major != 10)
+      return fail(ANVIL_E_UNSUPPORTED, "device %d is sm_%d%d; libanvil_cuda is built for sm_100a (B200)", dev,
+                  prop.major, prop.minor);
+    int rc = kernel_attrs(dev);
+    if (rc) return rc;
+    uint32_t *ptr = nullptr;
+    CK(cudaGetSymbolAddress((void **)&ptr, g_noalloc_scratch));
+    sm_count[dev] = prop.multiProcessorCount;
+    scratch_ptr[dev] = ptr;
+  }
+  anvil_model m;                                   // a host-side view only: no stream, arena or consts are created
+  m.device = dev;
+  m.sms = sm_count[dev];
+  m.stream = static_cast<cudaStream_t>(stream);
+  m.flags = scratch_ptr[dev];
+  Launch L;
+  memset(&L.op, 0, sizeof L.op);
+  L.op.kind = ANVIL_OP_GEMM;
+  L.op.flags = flags & (ANVIL_F_CHECKED | ANVIL_F_SIMT);
+  L.op.out_bytes = 1;
+  L.op.dims[0] = 1; L.op.dims[1] = M; L.op.dims[2] = N; L.op.dims[3] = K;
+  L.op.strides[3] = N;
+  L.op.mult = mult;
+  L.op.shift = shift;
+  for (int s = 0; s < 8; ++s) L.op.off[s] = ANVIL_LOC_NONE;
+  GemmParams &p = L.gp;
+  memset(&p, 0, sizeof p);
+  p.batch = 1; p.M = M; p.N = N; p.K = K;
+  p.o_rstride = N;
+  p.o_cstride = 1;
+  p.A = A; p.BT = BT; p.out = out;
+  p.mult = mult; p.shift = shift; p.out_bytes = 1;
+  p.check = (flags & ANVIL_F_CHECKED) ? 1 : 0;
+  p.flags = m.flags;
+  L.tc = !(flags & ANVIL_F_SIMT) && K % 16 == 0 && aligned16(A) && aligned16(BT);
+  if (L.tc) {
+    L.bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
+    p.m_tiles = (M + TC_BM - 1) / TC_BM;
+    p.n_tiles = (N + L.bn - 1) / L.bn;
+    p.tiles = p.m_tiles * p.n_tiles;
+    int rc;
+    if ((rc = make_map_i8(&L.mapA, A, K, M, 1, K, M * K, TC_BM))) return rc;
+    if ((rc = make_map_i8(&L.mapB, BT, K, N, 1, K, N * K, L.bn))) return rc;
+  }
+  // the array keeps the previous call's words: clear them before this call's kernel can raise any
+  CK(cudaMemsetAsync(m.flags, 0, FLAG_WORDS * sizeof(uint32_t), m.stream));
+  int rc = launch_op(&m, L);
+  if (rc) return rc;
+  uint32_t h[FLAG_WORDS];
+  CK(cudaMemcpyAsync(h, m.flags, sizeof h, cudaMemcpyDeviceToHost, m.stream));
+  CK(cudaStreamSynchronize(m.stream));
+  return check_flags(&m, h);
 }

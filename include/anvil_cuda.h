@@ -161,6 +161,19 @@ ANVIL_API void anvil_model_free(anvil_model *m);
 ANVIL_API int anvil_gemm_requant(const int8_t *A, const int8_t *BT, int8_t *out, int64_t M, int64_t N, int64_t K,
                        int32_t mult, int32_t shift, uint32_t flags, void *stream);
 
+/* anvil_gemm_requant without any device allocation. No counterpart in the reference: it exists for callers of
+ * this library that cannot allocate device memory themselves or let a library do it (a host framework that owns
+ * every device allocation, a process where cudaMalloc is not permitted). Same arguments, result and error codes as
+ * anvil_gemm_requant; the caller passes A, BT and out. The kernel's only other device memory is a file-scope
+ * static array of 16 32-bit words (64 bytes) that every GPU loading the library holds until the process exits; the
+ * GEMM uses 4 of them as its overflow / index / timeout status words and the call fails with ANVIL_E_BAD_ARG if it
+ * ever needed more than the array holds. The first call on a device does a one-time set-up there (it looks up the
+ * array's device address and the kernels' shared-memory limits), so make that first call before any stream capture.
+ * All calls share the array: it is cleared at the start of each call, and calls that overlap on the GPU (other
+ * streams, other host threads) race on it. The call synchronises `stream` before it returns. */
+ANVIL_API int anvil_gemm_requant_noalloc(const int8_t *A, const int8_t *BT, int8_t *out, int64_t M, int64_t N,
+                                         int64_t K, int32_t mult, int32_t shift, uint32_t flags, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
