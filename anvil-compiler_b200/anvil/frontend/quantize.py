@@ -15,8 +15,10 @@ Extensions for the nanoGPT family (the reference frontend rejects these, anvil/f
 476-478):
   * linear bias: bias_q = round(b / (s_in s_w)) as an i32 const added to the accumulator (qlinear's `bias`
     operand); an all-zero quantized bias is dropped, leaving exactly the reference's qlinear.
-  * layernorm: layernorm_int = rmsnorm_int on the mean-centred row (its LUT built by rmsnorm_lut for entries up
-    to twice the input magnitude), the LayerNorm bias quantized at the output scale as an i8 bias.
+  * layernorm: layernorm_int = rmsnorm_int on the mean-centred row, with the constants of the reference's wide
+    recipe (rmsnorm_lut_wide: eps folded into the sum as ss_init, an eps-free rsqrt LUT, exact at every
+    normalisation shift) for entries up to twice the input magnitude; the LayerNorm bias quantized at the output
+    scale as an i8 bias.
   * gelu: a 256-entry int8 LUT (the reference's silu_lut recipe with GELU) as a `lut` op; the cuda target fuses
     it into the producing qlinear's epilogue.
   * embed: wte and wpe each quantized per tensor; (Ma, Mb, s) from fixed_point as for a residual add.
@@ -186,9 +188,11 @@ def quantize(fg, calib_inputs, headroom=HEADROOM, *, names=None, softmax_one=SOF
             if dt[n.inputs[0].name] == "i8" and not center:
                 lut, s = rmsnorm_lut(sc_in[0], sw, so, wmax, d, n.attrs["eps"], rsqrt_len)
                 c = e = 0
-            elif dt[n.inputs[0].name] == "i8":
-                lut, s = rmsnorm_lut(sc_in[0], sw, so, wmax, d, n.attrs["eps"], rsqrt_len, mag=2 * mx)
-                c = e = 0
+            elif center:
+                # layernorm: eps folded into the sum (ss_init) with an eps-free LUT, exact at every
+                # normalisation shift k; the eps-in-the-LUT form adds 4^k eps at shift k, which is large for
+                # the small activations of N(0, 0.02)-initialised embeddings (anvil/frontend/quantize.py:122-128)
+                lut, s, c, e = rmsnorm_lut_wide(sc_in[0], sw, so, wmax, d, n.attrs["eps"], 2 * mx, rsqrt_len)
             else:
                 lut, s, c, e = rmsnorm_lut_wide(sc_in[0], sw, so, wmax, d, n.attrs["eps"], (2 if center else 1) * mx,
                                                 rsqrt_len)
