@@ -48,6 +48,8 @@ class CudaParams:
     def __post_init__(self):
         if not self.devices or any(not isinstance(d, int) or d < 0 for d in self.devices):
             raise ValueError(f"CudaParams.devices = {self.devices!r}: need non-negative ints")
+        if len(set(self.devices)) != len(self.devices):
+            raise ValueError(f"CudaParams.devices = {self.devices!r}: a device may appear once")
         if self.gemm not in ("auto", "tc", "simt"):
             raise ValueError(f"CudaParams.gemm = {self.gemm!r}: auto, tc or simt")
 
@@ -265,20 +267,27 @@ class CompiledModel:
         dt = self.in_dtypes.get(sym, "i8")
         bits = {"i8": 8, "i16": 16, "i32": 32}[dt]
         lo, hi = -(1 << (bits - 1)), (1 << (bits - 1)) - 1
+        info = np.iinfo(v.dtype) if v.dtype.kind in "iu" else None
+        if info is not None and info.min >= lo and info.max <= hi:
+            return v                              # the array's dtype cannot hold an out-of-range value
         if v.size and (int(v.min()) < lo or int(v.max()) > hi):
             raise ValueError(f"input {sym!r}: values in [{v.min()}, {v.max()}] outside {dt} [{lo}, {hi}]")
         return v
 
     # --------------------------------------------------------------------------------------------- runs
-    def run(self, x, backend: str = "cuda", *, quantized=False, keep="outputs", timing=False) -> RunOutput:
-        """Quantize `x` (unless quantized=True), run the launch chain on the GPU(s), read back."""
+    def run(self, x, backend: str = "cuda", *, quantized=False, keep="outputs", timing=False, out=None) -> RunOutput:
+        """Quantize `x` (unless quantized=True), run the launch chain on the GPU(s), read back. `out` may map graph
+        output syms to caller-owned C-contiguous arrays of the output's dtype and (batch,) + shape (pinned memory
+        makes the read-back a DMA at full bus speed); those outputs are written there and returned as those
+        arrays."""
         if backend not in BACKENDS:
             raise ValueError(f"unknown backend {backend!r}: this build runs {', '.join(BACKENDS)} (the tiny-gpu "
                              "simulators isasim/rtl/verilator are not part of it)")
         if keep not in ("outputs", "all"):
             raise ValueError(f"keep must be 'outputs' or 'all', not {keep!r}")
         bound, batch, batched = self._bind_inputs(x, quantized)
-        ints, kus, shards = self._run_cuda(bound, batch, keep, timing)
+        out = self._check_out(out, batch)
+        ints, kus, shards = self._run_cuda(bound, batch, keep, timing, out)
         if not batched:
             ints = {k: v[0] if v.ndim and v.shape[0] == 1 and k not in self._const_syms() else v
                     for k, v in ints.items()}
@@ -287,6 +296,20 @@ class CompiledModel:
         for d, us in zip(prog.devops, kus if kus is not None else [None] * len(prog.devops)):
             cycles[d.label] = (cycles.get(d.label) or 0) + us if us is not None else None
         return RunOutput(self, ints, cycles, CudaRunResult(batch, shards, cycles), prog)
+
+    def _check_out(self, out, batch):
+        if not out:
+            return {}
+        from .runtime.program import NP
+        for sym, arr in out.items():
+            if sym not in self.outputs:
+                raise ValueError(f"out: {sym!r} is not a graph output ({self.outputs})")
+            want = (batch,) + tuple(self.meta[sym][1])
+            if not isinstance(arr, np.ndarray) or arr.shape != want or arr.dtype != NP[self.meta[sym][2]] or \
+                    not arr.flags.c_contiguous or not arr.flags.writeable:
+                raise ValueError(f"out[{sym!r}] must be a writable C-contiguous {NP[self.meta[sym][2]].__name__} "
+                                 f"array of shape {want}")
+        return out
 
     def _const_syms(self):
         return {op.sym_str for op in self.func.ops if isinstance(op, g.ConstOp)}
@@ -303,13 +326,14 @@ class CompiledModel:
             lo = hi
         return out
 
-    def _run_cuda(self, bound, batch, keep, timing):
+    def _run_cuda(self, bound, batch, keep, timing, out=None):
         shards = self._shards(batch)
         results, errors = [None] * len(shards), [None] * len(shards)
 
         def work(i, dev, lo, hi):
             try:
-                results[i] = self._run_shard(dev, {k: v[lo:hi] for k, v in bound.items()}, hi - lo, keep, timing)
+                results[i] = self._run_shard(dev, {k: v[lo:hi] for k, v in bound.items()}, hi - lo, keep, timing,
+                                             {k: v[lo:hi] for k, v in (out or {}).items()})
             except BaseException as e:            # re-raised on the calling thread
                 errors[i] = e
 
@@ -329,11 +353,14 @@ class CompiledModel:
                 raise e
         ints = {}
         for k in results[0][0]:
+            if out and k in out:
+                ints[k] = out[k]                      # the shards were written in place
+                continue
             parts = [r[0][k] for r in results]
-            ints[k] = parts[0] if k in self._const_syms() else np.concatenate(parts, axis=0)
+            ints[k] = parts[0] if k in self._const_syms() or len(parts) == 1 else np.concatenate(parts, axis=0)
         return ints, results[0][1], [(d, hi - lo) for d, lo, hi in shards]
 
-    def _run_shard(self, device, bound, b, keep, timing):
+    def _run_shard(self, device, bound, b, keep, timing, out=None):
         prog = self.program(b, keep)
         dm = self._device_model(device)
         if dm.prepared_key != (b, keep):
@@ -343,18 +370,26 @@ class CompiledModel:
             arr = np.ascontiguousarray(bound[sym], dtype={"i8": np.int8, "i16": np.int16, "i32": np.int32}[dtype])
             ins.append((off, arr))
         want = self._readable(prog, keep)
-        roots = {}
+        roots, direct, outs = {}, {}, []
         for sym, v in want.items():
-            roots.setdefault(v.root, None)
-        outs = []
+            if out and sym in out and v.contiguous and out[sym].nbytes == prog.buffers[v.root]:
+                direct[sym] = out[sym]            # DMA straight into the caller's buffer
+                outs.append((prog.plan.addresses[v.root], out[sym]))
+            else:
+                roots.setdefault(v.root, None)
         for r in roots:
             buf = np.empty(prog.buffers[r], dtype=np.uint8)
             roots[r] = buf
             outs.append((prog.plan.addresses[r], buf))
         kus = dm.run(ins, outs, timing=timing)
-        ints = {}
+        ints = dict(direct)
         for sym, v in want.items():
+            if sym in direct:
+                continue
             ints[sym] = _apply_view(roots[v.root], v)
+            if out and sym in out:
+                out[sym][...] = ints[sym]
+                ints[sym] = out[sym]
         for sym in self.inputs:
             ints.setdefault(sym, bound[sym])
         return ints, kus

@@ -9,11 +9,14 @@ collective on the data path.
 ours (default) prints one JSON line with
   value         whole-job tokens/s with the inputs already in HBM: K steps of the launch chain (CUDA-graph replay of
                 every kernel) timed with CUDA events on the model's stream, max over ranks
-  e2e           the same metric through the public API, cm.run(x_int8, "cuda", quantized=True): per step the H2D
-                copy of the quantized input from pinned memory, every kernel, the D2H read of the output
-  roofline      the dominant kernel family (the tcgen05 GEMMs): algorithmic int8 ops per launch / average launch
-                time (CUDA events per launch on the model's stream), against 2 x the measured dense bf16 peak
-                (int8 dense rate = 2 x bf16 on B200); traffic from an ncu capture when one is committed
+  e2e           the same metric through the public API, cm.run(x_int8, "cuda", quantized=True, out=...): per step
+                the H2D copy of the quantized input from pinned memory, every kernel, the D2H read of the output
+                into a pinned buffer the caller owns
+  roofline      the dominant kernel family of the step: algorithmic int8 ops (or bytes) per launch / average
+                launch time (CUDA events per launch on the model's stream), against 2 x the measured dense bf16
+                peak (int8 dense rate = 2 x bf16 on B200) or the measured copy bandwidth; traffic from the
+                committed ncu summary; roofline_int8_gemm gives the same for the tcgen05 GEMMs
+  gemm_sweep_c4 config c4 (the int8 GEMM + requant sweep) through anvil_gemm_requant, sampled rows bit-exact
   cpu_baseline  the oracle port (numpy restatement of anvil.interp) on rank 0 at N = 1, one bounded sample
   clocks        nvidia-smi samples taken during the timed region
 --impl reference times that CPU oracle alone (rank 0), with a process pool over all host cores.
@@ -50,52 +53,54 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons every 200 ms on a background thread (the recipe's clocks line)."""
+    """SM clock and throttle reasons sampled during the timed region: NVML every ~5 ms on a background thread
+    (the recipe's nvidia-smi clocks line, at a rate a millisecond-scale region can catch), nvidia-smi as fallback."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
     def __init__(self, device):
-        self.device, self.rows, self.proc = device, [], None
+        self.device, self.sm, self.max, self.reasons, self._stop = device, [], None, set(), False
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(vis.split(",")[self.device]) if vis else self.device
+            self.h, self.nv = nv.nvmlDeviceGetHandleByIndex(idx), nv
+            self.max = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+        except Exception:
+            self.nv = None
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+    def _run(self):
+        while not self._stop:
+            if self.nv is not None:
+                try:
+                    self.sm.append(float(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)))
+                    r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                    self.reasons |= {k for k, bit in self.REASONS.items() if r & bit}
+                except Exception:
+                    self.nv = None
+            time.sleep(0.005)
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
+        self._stop = True
+        self.t.join(timeout=2)
+        if not self.sm:                          # NVML unavailable: one nvidia-smi reading
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+                out = subprocess.run(["nvidia-smi", f"--id={self.device}", "--query-gpu=clocks.sm,clocks.max.sm",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=20).stdout.split(",")
+                self.sm, self.max = [float(out[0])], float(out[1])
+            except Exception:
+                pass
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
-                for nm, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(nm)
-            except (ValueError, IndexError):
-                continue
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.max,
+                "reasons": sorted(self.reasons), "samples": len(self.sm)}
 
 
 def _dist():
@@ -283,27 +288,24 @@ def run_ours(args):
     for _ in range(2):
         kus2 = dm.run([(off, xin)], [], timing=True)
         kus = [min(a, b) for a, b in zip(kus, kus2)]
-    gemm_ops = sum(d.work.get("ops", 0) for d in prog.devops if d.kind == C.OP_GEMM)
-    gemm_us = sum(u for d, u in zip(prog.devops, kus) if d.kind == C.OP_GEMM)
-    n_gemm = sum(1 for d in prog.devops if d.kind == C.OP_GEMM)
-    by_kind = {}
-    for d, u in zip(prog.devops, kus):
-        k = C.KIND_NAMES[d.kind]
-        by_kind[k] = by_kind.get(k, 0.0) + u
     hbm, bf16, src = _peaks()
-    peak_tops = 2 * bf16
-    achieved = gemm_ops / (gemm_us * 1e-6) / 1e12 if gemm_us else 0.0
-    roofline = {"bound": "tensor", "kernel": "qgemm_tc (tcgen05 kind::i8)", "achieved": achieved,
-                "peak": peak_tops, "unit": "TOP/s", "frac": achieved / peak_tops,
-                "peak_source": f"2 x {src} bf16_tflops {bf16} (dense int8 = 2 x bf16 on B200)",
-                "ops_per_launch": gemm_ops / max(1, n_gemm), "avg_launch_us": gemm_us / max(1, n_gemm),
-                "traffic": _traffic_from_profiles(), "launches_per_step": n_gemm}
-    # e2e through the public API
+    roofs = _rooflines(prog, kus, hbm, bf16, src, C)
+    by_kind = {k: round(r["total_us"], 2) for k, r in roofs.items()}
+    dominant = max(roofs, key=lambda k: roofs[k]["total_us"])
+    roofline = {k: v for k, v in roofs[dominant].items() if k != "total_us"}
+    roofline["traffic"] = _traffic_from_profiles(dominant)
+    gemm_roof = {k: v for k, v in roofs["gemm"].items() if k != "total_us"} if "gemm" in roofs else None
+    # e2e through the public API: quantized input from pinned memory, the output read back into pinned memory
+    outs = {}
+    for s in cm.outputs:
+        shape, dt = (batch,) + tuple(cm.meta[s][1]), cm.meta[s][2]
+        outs[s] = torch.empty(shape, dtype={"i8": torch.int8, "i16": torch.int16, "i32": torch.int32}[dt],
+                              pin_memory=True).numpy()
     e2e_times = []
     for step in range(args.warmup + args.steps):
         torch.cuda.synchronize()
         t = time.perf_counter()
-        res = cm.run(xin, "cuda", quantized=True)
+        res = cm.run(xin, "cuda", quantized=True, out=outs)
         e2e_times.append(time.perf_counter() - t)
     e2e_s = statistics.mean(e2e_times[args.warmup:])
     e2e_s = _max_over_ranks(dist, e2e_s, f"cuda:{local}")
@@ -319,9 +321,12 @@ def run_ours(args):
             "e2e": {"value": ws * tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(xin.nbytes),
                     "d2h_bytes_per_step": int(out_bytes)},
             "roofline": roofline,
-            "kernel_us_by_kind": {k: round(v, 2) for k, v in sorted(by_kind.items(), key=lambda kv: -kv[1])},
+            "roofline_int8_gemm": gemm_roof,
+            "kernel_us_by_kind": dict(sorted(by_kind.items(), key=lambda kv: -kv[1])),
             "gpu_launches": sum(1 for d in prog.devops if d.kind != C.OP_COPY) * args.steps,
             "clocks": clk.summary()}
+    if rank == 0 and not args.no_sweep:
+        line["gemm_sweep_c4"] = gemm_sweep(2 * bf16)
     if rank == 0 and ws == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(cfg, cm, gen)
     if rank == 0:
@@ -332,12 +337,78 @@ def run_ours(args):
     return 0
 
 
-def _traffic_from_profiles():
-    """DRAM bytes per GEMM launch from the committed ncu summary, if there is one (else null)."""
+def _rooflines(prog, kus, hbm, bf16, src, C):
+    """Per kernel family: algorithmic ops (tensor-bound families) or bytes (HBM-bound) per launch over the average
+    CUDA-event launch time, against 2 x measured bf16 (dense int8) or the measured copy bandwidth."""
+    fam = {}
+    for d, u in zip(prog.devops, kus):
+        k = C.KIND_NAMES[d.kind]
+        f = fam.setdefault(k, {"n": 0, "us": 0.0, "ops": 0, "bytes": 0})
+        f["n"] += 1
+        f["us"] += u
+        f["ops"] += d.work.get("ops", 0)
+        f["bytes"] += d.work.get("bytes", 0)
+    out = {}
+    for k, f in fam.items():
+        avg = f["us"] / f["n"]
+        if f["ops"]:
+            ach = f["ops"] / f["n"] / (avg * 1e-6) / 1e12
+            peak, unit, bound = 2 * bf16, "TOP/s", "tensor"
+            ps = f"2 x {src} bf16_tflops {bf16} (dense int8 = 2 x dense bf16 on B200)"
+            per = {"ops_per_launch": f["ops"] / f["n"]}
+        else:
+            ach = f["bytes"] / f["n"] / (avg * 1e-6) / 1e9
+            peak, unit, bound = hbm, "GB/s", "hbm"
+            ps = f"{src} hbm_gbs {hbm}"
+            per = {"bytes_per_launch": f["bytes"] / f["n"]}
+        out[k] = {"kernel": k, "bound": bound, "achieved": ach, "peak": peak, "unit": unit, "frac": ach / peak,
+                  "peak_source": ps, "avg_launch_us": avg, "launches_per_step": f["n"], "total_us": f["us"], **per}
+    return out
+
+
+def gemm_sweep(peak_tops, reps=5):
+    """Config c4: int8 GEMM + requant at M in {1024, 8192, 65536}, K = N in {768, 3072, 4096} through
+    anvil_gemm_requant on device-resident operands; TOP/s from CUDA events, and 8 sampled rows per shape checked
+    bit-exact against the oracle."""
+    import torch
+    from anvil import workloads as W
+    from anvil.runtime import cuda as C
+    from oracle import semantics as osem
+    res = []
+    for m, k, n in W.GEMM_SWEEP:
+        a, b, mult, s = W.gemm_case(m, k, n)
+        ta = torch.from_numpy(a).cuda()
+        tbt = torch.from_numpy(np.ascontiguousarray(b.T)).cuda()
+        out = torch.empty((m, n), dtype=torch.int8, device="cuda")
+        st = torch.cuda.current_stream()
+        call = lambda: C.gemm_requant(ta.data_ptr(), tbt.data_ptr(), out.data_ptr(), m, n, k, mult, s, 0,  # noqa
+                                      st.cuda_stream)
+        for _ in range(3):
+            call()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(reps):
+            call()
+        e1.record(st)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000 / reps
+        rows = np.random.default_rng(m + k).choice(m, 8, replace=False)
+        want = osem.requant(osem.matmul_i8(a[rows].astype(np.int64), b.astype(np.int64)), mult, s)
+        exact = bool(np.array_equal(out.cpu().numpy()[rows].astype(np.int64), want))
+        tops = 2 * m * n * k / (us * 1e-6) / 1e12
+        res.append({"M": m, "K": k, "N": n, "us": round(us, 2), "tops": round(tops, 1),
+                    "frac": round(tops / peak_tops, 4), "rows_exact": exact})
+        del ta, tbt, out
+    return res
+
+
+def _traffic_from_profiles(kind):
+    """DRAM bytes (read + write) per launch of `kind` from the committed ncu summary, if there is one."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(p):
         with open(p) as f:
-            return json.load(f).get("qgemm_tc_bytes_per_launch")
+            return json.load(f).get(kind)
     return None
 
 
@@ -351,6 +422,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--max-workers", type=int, default=64)
+    ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--skip-check", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -202,3 +202,17 @@ def test_random_graphs_unchecked_fused(seed):
     cm = anvil.compile(m, consts=c, prove=False, params=CudaParams(checked=False))
     res = cm.run([x[s] for s in cm.inputs], "cuda", quantized=True)
     _check(res.ints, want.values, cm.outputs)
+
+
+def test_out_buffers_receive_the_outputs():
+    module, consts, body = _frozen()
+    rng = np.random.default_rng(9)
+    xs = rng.integers(-(1 << 15), 1 << 15, (16,) + np.shape(body["x"]))
+    want = interp.run(module, {"x": xs}, consts, batch=True)
+    cm = anvil.compile(module, consts=consts)
+    o = cm.outputs[0]
+    buf = np.zeros((16,) + tuple(cm.meta[o][1]), dtype=np.int16)
+    res = cm.run(xs, "cuda", quantized=True, out={o: buf})
+    assert res.ints[o] is buf and np.array_equal(buf, want.values[o])
+    with pytest.raises(ValueError):
+        cm.run(xs, "cuda", quantized=True, out={o: np.zeros((16, 3), dtype=np.int16)})
