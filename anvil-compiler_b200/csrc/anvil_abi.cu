@@ -247,6 +247,25 @@ static int resolve(anvil_model *m, const anvil_op &op, int slot, uint64_t bytes,
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// tc GEMMs with i8 row-major outputs of 256-column tiles store through TMA (32 rows x 128 bytes per epilogue warp);
+// the tensor map goes in L.mapC and sets gp.tma_store. Other outputs keep the per-lane global stores.
+static int gemm_out_map(Launch &L) {
+  GemmParams &p = L.gp;
+  memset(&L.mapC, 0, sizeof L.mapC);
+  p.tma_store = 0;
+  if (!L.tc || L.bn != 256 || p.out_bytes != 1 || p.o_cstride != 1 || p.o_group != 0 || !aligned16(p.out) ||
+      p.o_rstride % 16 != 0 || (p.batch > 1 && p.o_bstride % 16 != 0) || p.M > (1ll << 31) - 1 ||
+      p.N > (1ll << 31) - 1)
+    return ANVIL_OK;
+  const uint64_t cdims[3] = {(uint64_t)p.N, (uint64_t)p.M, (uint64_t)p.batch};
+  const uint64_t cstr[2] = {(uint64_t)p.o_rstride, (uint64_t)p.o_bstride};
+  const uint32_t cbox[3] = {128, 32, 1};
+  int rc = make_map(&L.mapC, p.out, p.batch > 1 ? 3 : 2, cdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  p.tma_store = 1;
+  return ANVIL_OK;
+}
+
 static int prepare_gemm(anvil_model *m, Launch &L) {
   const anvil_op &op = L.op;
   const int64_t batch = op.dims[0], M = op.dims[1], N = op.dims[2], K = op.dims[3];
@@ -254,6 +273,8 @@ static int prepare_gemm(anvil_model *m, Launch &L) {
   if (batch < 1 || M < 1 || N < 1 || K < 1) return fail(ANVIL_E_BAD_ARG, "op %d: bad gemm dims", op.op_index);
   if (op.out_bytes != 1 && op.out_bytes != 2) return fail(ANVIL_E_BAD_ARG, "op %d: gemm output must be i8 or i16", op.op_index);
   if (op.shift < 0 || op.shift > 31) return fail(ANVIL_E_BAD_ARG, "op %d: shift %lld outside [0, 31]", op.op_index, (long long)op.shift);
+  if ((op.flags & ANVIL_F_LUT) && op.out_bytes != 1)
+    return fail(ANVIL_E_BAD_ARG, "op %d: a LUT epilogue needs an i8 result", op.op_index);
   const int64_t o_grp = op.strides[4], o_gs = op.strides[5], o_cs = op.strides[6] ? op.strides[6] : 1;
   if (a_bs < 0 || bt_bs < 0 || o_bs < 0 || o_rs < 0 || o_grp < 0 || o_gs < 0 || o_cs < 1 ||
       (o_cs == 1 && o_rs < N))
@@ -317,7 +338,7 @@ static int prepare_gemm(anvil_model *m, Launch &L) {
   const uint64_t b_z = bt_bs ? batch : 1, b_zs = bt_bs ? bt_bs : N * K;
   if ((rc = make_map_i8(&L.mapA, p.A, K, M, a_z, K, a_zs, TC_BM))) return rc;
   if ((rc = make_map_i8(&L.mapB, p.BT, K, N, b_z, K, b_zs, L.bn))) return rc;
-  return ANVIL_OK;
+  return gemm_out_map(L);
 }
 
 // ATTENTION: dims = {B, H, T1, T2, hd}; strides = {q_b, q_h, q_t, k_b, k_h, k_t, o_b, o_t};
@@ -489,8 +510,10 @@ static int launch_op(anvil_model *m, Launch &L) {
         const int grid = (int)std::min<int64_t>(p.tiles, m->sms);
 #define TC_LAUNCH(BN, OB)                                                                                       \
   do {                                                                                                          \
-    if (p.res) qgemm_tc_kernel<BN, OB, true><<<grid, TC_THREADS, TcCfg<BN>::SMEM_BYTES, st>>>(L.mapA, L.mapB, p);  \
-    else qgemm_tc_kernel<BN, OB, false><<<grid, TC_THREADS, TcCfg<BN>::SMEM_BYTES, st>>>(L.mapA, L.mapB, p);       \
+    if (p.res)                                                                                                  \
+      qgemm_tc_kernel<BN, OB, true><<<grid, TC_THREADS, TcCfg<BN>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, p); \
+    else                                                                                                        \
+      qgemm_tc_kernel<BN, OB, false><<<grid, TC_THREADS, TcCfg<BN>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, p);\
   } while (0)
         if (L.bn == 64) { if (op.out_bytes == 1) TC_LAUNCH(64, 1); else TC_LAUNCH(64, 2); }
         else if (L.bn == 128) { if (op.out_bytes == 1) TC_LAUNCH(128, 1); else TC_LAUNCH(128, 2); }
@@ -776,6 +799,7 @@ extern "C" int anvil_gemm_requant(const int8_t *A, const int8_t *BT, int8_t *out
     int rc;
     if ((rc = make_map_i8(&L.mapA, A, K, M, 1, K, M * K, TC_BM))) return rc;
     if ((rc = make_map_i8(&L.mapB, BT, K, N, 1, K, N * K, L.bn))) return rc;
+    if ((rc = gemm_out_map(L))) return rc;
   }
   cudaStream_t saved = m->stream;
   m->stream = static_cast<cudaStream_t>(stream);
@@ -863,6 +887,7 @@ extern "C" int anvil_gemm_requant_noalloc(const int8_t *A, const int8_t *BT, int
     int rc;
     if ((rc = make_map_i8(&L.mapA, A, K, M, 1, K, M * K, TC_BM))) return rc;
     if ((rc = make_map_i8(&L.mapB, BT, K, N, 1, K, N * K, L.bn))) return rc;
+    if ((rc = gemm_out_map(L))) return rc;
   }
   // the array keeps the previous call's words: clear them before this call's kernel can raise any
   CK(cudaMemsetAsync(m.flags, 0, FLAG_WORDS * sizeof(uint32_t), m.stream));

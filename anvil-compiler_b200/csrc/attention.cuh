@@ -85,7 +85,6 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
       : "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // byte offset of 16-byte chunk `ch` (0..7) of row `r` (0..127) inside one 128 x 128 P slab (SW128 K-major)
 __device__ __forceinline__ int pslab_off(int r, int ch) { return (r >> 3) * 1024 + (r & 7) * 128 + ((ch ^ (r & 7)) << 4); }
@@ -99,7 +98,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
                 const __grid_constant__ CUtensorMap mapV, const AttnParams p) {
   using Cfg = AttnCfg<HD>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *smem = align_smem_1024(smem_raw);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::OFF_BAR);
   uint64_t *qfull = bars;
   uint64_t *rfull = qfull + 1, *rempty = rfull + Cfg::NS;
@@ -128,7 +127,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     *abort = 0;
     fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < 256 * Cfg::LUT_COPIES; i += blockDim.x) lut[i] = p.lut[i / Cfg::LUT_COPIES];
+  for (int i = threadIdx.x; i < 64 * Cfg::LUT_COPIES; i += blockDim.x) {
+    const int32_t e = __ldg(p.lut + (4 * i) / Cfg::LUT_COPIES);
+    reinterpret_cast<int4 *>(lut)[i] = make_int4(e, e, e, e);
+  }
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
@@ -146,7 +148,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       // ring sequence g: K tiles 0..nkv-1, then V^T slabs 0..nkv-1 (the V loads land while the softmax runs)
       for (int g = 0; g < 2 * nkv && ok; ++g) {
         const int st = g % Cfg::NS;
-        if (!mbar_wait(&rempty[st], ((g / Cfg::NS) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
+        if (!mbar_wait_idle(&rempty[st], ((g / Cfg::NS) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
         mbar_arrive_expect_tx(&rfull[st], Cfg::T_BYTES);
         uint8_t *dst = smem + Cfg::OFF_R + st * Cfg::T_BYTES;
         if (g < nkv) tma_load_4d(dst, &mapK, 0, h, g * 128, b, &rfull[st]);
@@ -180,7 +182,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         mma_commit(&rempty[st]);
         mma_commit(&sfull[sb]);
       }
-      if (ok) ok = mbar_wait(pready, 0, abort, p.flags, p.op_index);
+      if (ok) ok = mbar_wait_idle(pready, 0, abort, p.flags, p.op_index);
       tc_fence_after();
       for (int j = 0; j < nkv && ok; ++j) {
         const int g = nkv + j, st = g % Cfg::NS;
@@ -211,7 +213,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int sb = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&sfull[sb], (j >> 1) & 1, abort, p.flags, p.op_index));
+      ok = __all_sync(0xffffffffu, mbar_wait_idle(&sfull[sb], (j >> 1) & 1, abort, p.flags, p.op_index));
       if (!ok) break;                       // warp-uniform: the TMEM load below is .sync.aligned
       tc_fence_after();
       int32_t acc[32];
@@ -232,8 +234,11 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         for (int q = 0; q < 32; ++q)
           if (cbase + q < kept) mx = max(mx, v[q]);
       }
+      // the slab holds each score biased by 128 (x + 128 as an unsigned byte), so both passes below read it
+      // with one zero-extending byte extract; pass B overwrites it with the probabilities
 #pragma unroll
-      for (int q = 0; q < 8; ++q) w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      for (int q = 0; q < 8; ++q)
+        w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]) ^ 0x80808080u;
       uint8_t *slab = pbuf + j * Cfg::P_SLAB;
       *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part)) = make_uint4(w[0], w[1], w[2], w[3]);
       *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
@@ -245,10 +250,11 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     asm volatile("bar.sync 1, 512;" ::: "memory");
     mx = max(max(red[r], red[128 + r]), max(red[256 + r], red[384 + r]));
     asm volatile("bar.sync 1, 512;" ::: "memory");
-    const int base_idx = 255 - mx;
-    const int32_t *lutc = lut + base_idx * Cfg::LUT_COPIES + lcopy;     // lutc[x * COPIES] = lut[x - max + 255]
+    // a kept score x <= mx is stored as u = x + 128, and lut[x - mx + 255] = lut[u + 127 - mx]: lutc[u * COPIES]
+    // is that entry in this lane's copy (index 0..255 for every kept u)
+    const int32_t *lutc = lut + (127 - mx) * Cfg::LUT_COPIES + lcopy;
     // pass A: partial S = sum over this part's kept columns of lut[x - max + 255]
-    int tot = 0;
+    int tot0 = 0, tot1 = 0;
     for (int j = 0; j < nkv && ok; ++j) {
       const uint8_t *slab = pbuf + j * Cfg::P_SLAB;
 #pragma unroll
@@ -258,34 +264,37 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           const uint4 v4 = *reinterpret_cast<const uint4 *>(slab + pslab_off(r, 2 * part + hh));
           const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
           if (c0 + 16 <= kept) {
+            // two independent three-input adds per word (each folds two entries into one accumulator)
 #pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              tot += lutc[sbyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES];
+            for (int q = 0; q < 4; ++q) {
+              tot0 += lutc[ubyte(wv[q], 0) * Cfg::LUT_COPIES] + lutc[ubyte(wv[q], 1) * Cfg::LUT_COPIES];
+              tot1 += lutc[ubyte(wv[q], 2) * Cfg::LUT_COPIES] + lutc[ubyte(wv[q], 3) * Cfg::LUT_COPIES];
             }
           } else {
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
-              if (c0 + q < kept) tot += lutc[sbyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES];
+              if (c0 + q < kept) tot0 += lutc[ubyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES];
             }
           }
         }
       }
     }
-    red[part * 128 + r] = tot;
+    red[part * 128 + r] = tot0 + tot1;
     asm volatile("bar.sync 1, 512;" ::: "memory");
-    tot = red[r] + red[128 + r] + red[256 + r] + red[384 + r];
+    const int tot = red[r] + red[128 + r] + red[256 + r] + red[384 + r];
     // pass B: p = floor((e*one + S/2) / S), masked entries 0. The division is a multiply by a per-row magic
     // number (Granlund & Montgomery, "Division by invariant integers using multiplication", 1994): with
     // l = ceil(log2 S), k = 31 + l and m = ceil(2^k / S) (m <= 2^32), floor(n m / 2^k) = floor(n / S) for every
     // 0 <= n < 2^31, because m S - 2^k < S <= 2^l makes the error term n (m S - 2^k) / (S 2^k) < 1 / S.
-    // With m < 2^32 this is a 32 x 32 -> high 32 multiply and a shift by l - 1; S = 1 (l = 0) passes n through.
+    // With m < 2^32 this is a 32 x 32 -> high 32 multiply and a shift by l - 1. S = 1 takes the same form with
+    // n doubled (one2 = 2*one, m = 2^31, shift 0): the high word of 2n * 2^31 is n (2n < 2^32 as e*one < 2^31).
     const int S = tot > 0 ? tot : 1;
-    const int half = tot >> 1;
     const int lg = S > 1 ? 32 - __clz(S - 1) : 0;
-    const unsigned magic = (unsigned)(((1ull << (31 + lg)) + (unsigned long long)(S - 1)) / (unsigned long long)S);
+    const unsigned magic =
+        S > 1 ? (unsigned)(((1ull << (31 + lg)) + (unsigned long long)(S - 1)) / (unsigned long long)S) : 0x80000000u;
     const int msh = lg > 0 ? lg - 1 : 0;
-    const bool s_is_one = S == 1;
-    const int one = p.one;
+    const unsigned one2 = S > 1 ? (unsigned)p.one : 2u * (unsigned)p.one;
+    const unsigned half2 = S > 1 ? (unsigned)(tot >> 1) : 2u * (unsigned)(tot >> 1);
     for (int j = 0; j < nkv && ok; ++j) {
       uint8_t *slab = pbuf + j * Cfg::P_SLAB;
 #pragma unroll
@@ -299,19 +308,18 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           int pv[16];
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            const unsigned num = (unsigned)(lutc[sbyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES] * one + half);
-            pv[q] = (int)(s_is_one ? num : (__umulhi(num, magic) >> msh));
+            const unsigned num = (unsigned)lutc[ubyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES] * one2 + half2;
+            pv[q] = (int)(__umulhi(num, magic) >> msh);
           }
 #pragma unroll
           for (int q = 0; q < 4; ++q) ov[q] = pack4_sat_s8(pv[4 * q], pv[4 * q + 1], pv[4 * q + 2], pv[4 * q + 3]);
         } else if (c0 < kept) {
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            const int x = (int)(int8_t)(wv[q >> 2] >> (8 * (q & 3)));
             unsigned pq = 0;
             if (c0 + q < kept) {
-              const unsigned num = (unsigned)(lutc[x * Cfg::LUT_COPIES] * one + half);
-              pq = s_is_one ? num : (__umulhi(num, magic) >> msh);
+              const unsigned num = (unsigned)lutc[ubyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES] * one2 + half2;
+              pq = __umulhi(num, magic) >> msh;
             }
             ov[q >> 2] |= (pq & 0xffu) << (8 * (q & 3));
           }
@@ -322,7 +330,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     fence_proxy_async();
     mbar_arrive(pready);
     // O = P V from TMEM -> requant -> merged-heads output row (parts 0 .. HD/32-1 take 32 columns each)
-    if (ok && part < HD / 32 && __all_sync(0xffffffffu, mbar_wait(ofull, 0, abort, p.flags, p.op_index))) {
+    if (ok && part < HD / 32 && __all_sync(0xffffffffu, mbar_wait_idle(ofull, 0, abort, p.flags, p.op_index))) {
       tc_fence_after();
       const long long rnd2 = round_term(p.s2);
       int32_t acc[32];

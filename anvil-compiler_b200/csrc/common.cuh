@@ -65,10 +65,20 @@ __device__ __forceinline__ uint32_t pack4_sat_s8(int a0, int a1, int a2, int a3)
 // Signed byte q (0..3) of w, sign-extended: always in [-128, 127].
 __device__ __forceinline__ int sbyte(uint32_t w, int q) { return (int)(int8_t)(w >> (8 * q)); }
 
+// Unsigned byte q (0..3) of w, zero-extended (one byte permute): always in [0, 255].
+__device__ __forceinline__ uint32_t ubyte(uint32_t w, int q) { return __byte_perm(w, 0u, 0x4440u | (uint32_t)q); }
+
 // ------------------------------------------------------------------------------------------------- PTX: misc
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// The dynamic shared-memory base rounded up to 1024 bytes by pointer arithmetic on the __shared__ array itself:
+// the compiler then keeps every pointer derived from it in the shared state space (ld/st.shared), where an
+// integer round trip would leave it generic (slower generic loads and stores, long-scoreboard waits).
+__device__ __forceinline__ uint8_t *align_smem_1024(uint8_t *raw) {
+  return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
 }
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -138,6 +148,38 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   }
 }
 
+// mbarrier.try_wait with a suspend-time hint: the thread sleeps until the phase completes or `hint_ns` passes.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait for long waits of a single elected thread (a producer or MMA issuer idle while other warps compute):
+// each try suspends the thread for up to 20 us instead of spinning, so it takes no issue slots from the warps
+// doing the work. Bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t *bar, uint32_t parity, volatile int *abort, uint32_t *flags,
+                                               int op_index) {
+  uint32_t a = smem_u32(bar);
+  if (mbar_try_wait(a, parity)) return true;
+  uint64_t t0 = globaltimer();
+  for (;;) {
+    if (mbar_try_wait_hint(a, parity, 20000u)) return true;
+    if (*abort) return false;
+    if (globaltimer() - t0 > ANVIL_DEV_WAIT_NS) {
+      *abort = 1;
+      raise_flag(flags, FLAG_TIMEOUT, op_index);
+      return false;
+    }
+  }
+}
+
 // Wait up to `ns` nanoseconds, ignoring the abort word (drains copies still in flight after an abort).
 __device__ __forceinline__ bool mbar_wait_ns(uint64_t *bar, uint32_t parity, uint64_t ns) {
   uint32_t a = smem_u32(bar);
@@ -157,6 +199,35 @@ __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *m
       "[%5];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Shared -> global tile stores (bulk-group completion). The writer threads make their shared-memory stores
+// visible to the async proxy (fence_proxy_async) before one thread issues the copy; the issuer waits with
+// bulk_wait_read before the staging buffer is written again and with bulk_wait_all before the CTA exits.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *smem_src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Orders this thread's generic shared-memory writes before later async-proxy reads (TMA stores, tcgen05.mma).
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void st_shared_v4(void *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {

@@ -39,6 +39,8 @@ struct GemmParams {
   const void *res;
   int res_bytes, y_bytes, shift2;
   int ma, mb;
+  // tc path: 1 = the output leaves through shared-memory staging and TMA tile stores (i8, row-major, BN = 256)
+  int tma_store;
 };
 
 // y -> the fused residual add's result (32-bit exact under the static int32 proof)
@@ -153,12 +155,17 @@ struct TcCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = TC_SMEM_RING / STAGE_BYTES > 8 ? 8 : TC_SMEM_RING / STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;     // two accumulators
-  // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2]; then the TMEM base slot and abort word, the LUT
-  // replicated once per lane (8 KB, conflict-free lookups), and a 128-byte bias staging slot per epilogue warp
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  // A LUT epilogue keeps the LUT replicated once per lane as int32 words (32 KB: entry e of lane l at word
+  // 32 e + l, conflict-free lookups) in the last LUT_STAGES ring stages, and runs with the rest of the ring.
+  static constexpr int LUT_STAGES = (32 * 1024 + STAGE_BYTES - 1) / STAGE_BYTES;
+  // After the ring: the output staging (one 32-row x 128-byte, 128-byte-swizzled tile per epilogue warp), the
+  // barriers full[S], empty[S], tmem_full[2], tmem_empty[2], the TMEM base slot and abort word, and a 128-byte
+  // bias staging slot per epilogue warp.
+  static constexpr int STG_OFF = STAGES * STAGE_BYTES;
+  static constexpr int STG_BYTES = TC_EPI_WARPS * 4096;
+  static constexpr int BAR_OFF = STG_OFF + STG_BYTES;
   static constexpr int MISC_OFF = BAR_OFF + (2 * STAGES + 4) * 8;
-  static constexpr int LUT_OFF = MISC_OFF + 16;
-  static constexpr int BST_OFF = LUT_OFF + 32 * 256;
+  static constexpr int BST_OFF = MISC_OFF + 16;
   static constexpr int SMEM_BYTES = BST_OFF + TC_EPI_WARPS * 128 + 1024;   // + 1 KB slack to align the ring
 };
 
@@ -223,17 +230,18 @@ __device__ __forceinline__ void store_row32(typename IntOf<OB>::T *dst, const in
 template <int BN, int OB, bool RES>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using Cfg = TcCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *smem = align_smem_1024(smem_raw);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + Cfg::BAR_OFF);
   uint64_t *empty = full + Cfg::STAGES;
   uint64_t *tfull = empty + Cfg::STAGES;
   uint64_t *tempty = tfull + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Cfg::MISC_OFF);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + Cfg::MISC_OFF + 4);
-  int8_t *lut_r = reinterpret_cast<int8_t *>(smem + Cfg::LUT_OFF);      // entry i of lane l's copy: (i/4)*128 + 4l + i%4
+  const int nst = p.lut ? Cfg::STAGES - Cfg::LUT_STAGES : Cfg::STAGES;   // ring stages in use
+  int32_t *lut_r = reinterpret_cast<int32_t *>(smem + nst * Cfg::STAGE_BYTES);   // entry e of lane l: word 32 e + l
   int32_t *bst = reinterpret_cast<int32_t *>(smem + Cfg::BST_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -252,12 +260,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (p.tma_store) prefetch_tmap(&tmC);
   }
   if (p.lut)
-    for (int i = threadIdx.x; i < 32 * 256; i += TC_THREADS) {
-      const int e = i & 255, l = i >> 8;
-      lut_r[(e >> 2) * 128 + l * 4 + (e & 3)] = p.lut[e];
-    }
+    for (int i = threadIdx.x; i < 32 * 256; i += TC_THREADS) lut_r[i] = p.lut[i >> 5];
   if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
@@ -283,11 +289,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
           tma_load_3d(sa, &tmA, kb * TC_BK, (int)(mb * TC_BM), (int)bb, &full[stage]);
           tma_load_3d(sb, &tmB, kb * TC_BK, (int)(nb * BN), p.bt_bstride ? (int)bb : 0, &full[stage]);
-          if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1u; }
+          if (++stage == nst) { stage = 0; phase ^= 1u; }
         }
       }
       if (!ok) {      // aborted: let every tile load already issued land before the CTA's smem is released
-        for (int s = 0; s < Cfg::STAGES; ++s)
+        for (int s = 0; s < nst; ++s)
           if (armed & (1u << s)) mbar_wait_ns(&full[s], (armed_phase >> s) & 1u, 10000000ull);
       }
     }
@@ -315,7 +321,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                    (kb > 0 || k > 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
-          if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1u; }
+          if (++stage == nst) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
         mma_commit(&tfull[acc]);
@@ -325,27 +331,59 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..9)
     // warp w reads TMEM lane quarter (w % 4) and columns [half*BN/2, half*BN/2 + BN/2), half = (w - 2) / 4
+    constexpr int NCH = BN / 64;                         // 32-column chunks per warp and tile
     const int lane_base = 32 * (warp & 3);
     const int half = (warp - 2) >> 2;
     int32_t *bslot = bst + (warp - 2) * 32;
     int acc = 0;
     uint32_t aphase = 0;
     constexpr int lo = OB == 1 ? -128 : -32768, hi = OB == 1 ? 127 : 32767;
-    const int8_t *lt = p.lut ? lut_r : nullptr;
+    const int32_t *lt = p.lut ? lut_r + lane : nullptr;       // this lane's copy: lt[32 e] = lut[e]
     const int m32 = (int)p.mult, sh = p.shift, rnd = sh ? 1 << (sh - 1) : 0;
+    // fused residual with i8 y and i8 residual: both enter biased by 128 (u = x + 128, one byte extract each),
+    // and -128 (Ma + Mb) folds into the rounding constant; the sum is formed mod 2^32 and is exact because the
+    // static int32 proof bounds the true value
+    const bool res_fast = RES && p.res_bytes == 1 && p.y_bytes == 1;
+    const int s2 = p.shift2;
+    // TMA-store epilogue: this warp's 32 rows x 128 columns of the tile are packed into its staging tile (row r
+    // at r*128 bytes, 16-byte chunk c at position c ^ (r & 7), the 128-byte swizzle of the output tensor map)
+    // and leave as one tile store; edges are clipped by the tensor map
+    const bool tma_st = p.tma_store != 0;
+    uint8_t *stg = smem + Cfg::STG_OFF + (warp - 2) * 4096 + lane * 128;
+    const uint32_t c2 = (uint32_t)(s2 ? 1 << (s2 - 1) : 0) - 128u * ((uint32_t)p.ma + (uint32_t)p.mb);
     bool bad = false;
     for (int64_t t = blockIdx.x; t < p.tiles; t += gridDim.x) {
       const int64_t nb = t % p.n_tiles, rest = t / p.n_tiles;
       const int64_t mb = rest % p.m_tiles, bb = rest / p.m_tiles;
-      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aphase, abort, p.flags, p.op_index))) break;
-      tc_fence_after();
       const int64_t row = mb * TC_BM + lane_base + lane;
       const bool row_ok = row < p.M;
+      // residual words of chunk c of this lane's row, issued one chunk ahead (the first before the accumulator
+      // wait) so the loads overlap the MMAs and the previous chunk's arithmetic
+      uint4 rcur[2], rnxt[2];
+      bool rcur_ok = false, rnxt_ok = false;
+      auto prefetch = [&](int ci, uint4(&dst)[2], bool &ok) {
+        const int64_t col0 = nb * BN + half * (BN / 2) + ci * 32;
+        const int8_t *src = reinterpret_cast<const int8_t *>(p.res) + row * p.N + col0;
+        ok = res_fast && row_ok && col0 + 32 <= p.N && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+        if (ok) {
+          dst[0] = reinterpret_cast<const uint4 *>(src)[0];
+          dst[1] = reinterpret_cast<const uint4 *>(src)[1];
+        }
+      };
+      if (RES) prefetch(0, rcur, rcur_ok);
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aphase, abort, p.flags, p.op_index))) break;
+      tc_fence_after();
+      if (tma_st) {                                    // the previous tile's store has read the staging tile
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
+      }
       using TO = typename IntOf<OB>::T;
       const int64_t R = p.o_group ? p.o_group : p.M;
       TO *orow = reinterpret_cast<TO *>(p.out) + bb * p.o_bstride + (row / R) * p.o_gstride + (row % R) * p.o_rstride;
 #pragma unroll 1
-      for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
+      for (int ci = 0; ci < NCH; ++ci) {
+        const int c0 = half * (BN / 2) + ci * 32;
+        if (RES && ci + 1 < NCH) prefetch(ci + 1, rnxt, rnxt_ok);
         int32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c0), r);
         const int64_t col0 = nb * BN + c0;
@@ -354,8 +392,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (p.check) {
 #pragma unroll
           for (int q = 0; q < 32; ++q)
-            v[q] = gemm_epi<true>(r[q], (p.bias && col0 + q < p.N) ? p.bias[col0 + q] : 0, p, lt ? p.lut : nullptr,
-                                  lo, hi, bad);
+            v[q] = gemm_epi<true>(r[q], (p.bias && col0 + q < p.N) ? p.bias[col0 + q] : 0, p, p.lut, lo, hi, bad);
         } else {
           // the static int32 proof holds: (acc [+ bias]) * M + 2^(s-1) fits int32, so 32-bit wrap-free math is
           // exact; a bias arrives pre-folded as bias*M + 2^(s-1) (ANVIL_F_BIAS_RND)
@@ -373,16 +410,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
             for (int q = 0; q < 32; ++q) br[q] = rnd;
           }
-          if (!RES) {
+          int y[32];
 #pragma unroll
-            for (int q = 0; q < 32; ++q) {
-              int x = (r[q] * m32 + br[q]) >> sh;
-              if (OB != 1 || lt) x = min(hi, max(lo, x));      // i8 without a LUT saturates in the pack
-              if (lt) {
-                const int e = x + 128;
-                x = lt[(e >> 2) * 128 + lane * 4 + (e & 3)];
+          for (int q = 0; q < 32; ++q) y[q] = (r[q] * m32 + br[q]) >> sh;
+          if (!RES) {
+            if (OB == 1 && lt) {
+              // saturate four at a time, bias the bytes by 128 and look each up in this lane's LUT copy
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const uint32_t w = pack4_sat_s8(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]) ^ 0x80808080u;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[4 * q + k] = lt[ubyte(w, k) * 32];
               }
-              v[q] = x;
+            } else {
+#pragma unroll
+              for (int q = 0; q < 32; ++q) v[q] = OB == 1 ? y[q] : min(hi, max(lo, y[q]));   // i8 saturates in the pack
+            }
+          } else if (rcur_ok) {
+            const uint4 *rw = rcur;
+            const uint32_t rwv[8] = {rw[0].x ^ 0x80808080u, rw[0].y ^ 0x80808080u, rw[0].z ^ 0x80808080u,
+                                     rw[0].w ^ 0x80808080u, rw[1].x ^ 0x80808080u, rw[1].y ^ 0x80808080u,
+                                     rw[1].z ^ 0x80808080u, rw[1].w ^ 0x80808080u};
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const uint32_t yw = pack4_sat_s8(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]) ^ 0x80808080u;
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const int x = (int)(ubyte(rwv[q], k) * (uint32_t)p.ma + ubyte(yw, k) * (uint32_t)p.mb + c2);
+                const int o = x >> s2;
+                v[4 * q + k] = OB == 1 ? o : min(hi, max(lo, o));
+              }
             }
           } else {          // fused residual add: y clamped to its own dtype, then res*Ma + y*Mb requantised
             const int ylo = p.y_bytes == 1 ? -128 : -32768, yhi = p.y_bytes == 1 ? 127 : 32767;
@@ -390,13 +447,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int cnt = (int)(p.N - col0 < 32 ? p.N - col0 : 32);
             if (row_ok) load_row32(p.res, p.res_bytes, row * p.N + col0, cnt, rv);
 #pragma unroll
-            for (int q = 0; q < 32; ++q) {
-              const int y = min(yhi, max(ylo, (r[q] * m32 + br[q]) >> sh));
-              v[q] = residual_add<OB>(y, row_ok ? rv[q] : 0, p);
-            }
+            for (int q = 0; q < 32; ++q) v[q] = residual_add<OB>(min(yhi, max(ylo, y[q])), row_ok ? rv[q] : 0, p);
           }
         }
-        if (row_ok) {
+        if (tma_st) {
+          uint32_t w[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          st_shared_v4(stg + (((2 * ci) ^ (lane & 7)) << 4), w[0], w[1], w[2], w[3]);
+          st_shared_v4(stg + (((2 * ci + 1) ^ (lane & 7)) << 4), w[4], w[5], w[6], w[7]);
+        } else if (row_ok) {
           const int cnt = (int)(p.N - col0 < 32 ? p.N - col0 : 32);
           if (p.o_cstride == 1) {
             store_row32<OB>(orow + col0, v, cnt);
@@ -407,11 +467,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               if (q < cnt) dst[q * p.o_cstride] = (TO)min(hi, max(lo, v[q]));
           }
         }
+        if (RES) {
+          rcur[0] = rnxt[0];
+          rcur[1] = rnxt[1];
+          rcur_ok = rnxt_ok;
+        }
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (++acc == 2) { acc = 0; aphase ^= 1u; }
+      if (tma_st) {
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          const uint8_t *src = smem + Cfg::STG_OFF + (warp - 2) * 4096;
+          const int x = (int)(nb * BN + half * (BN / 2)), y = (int)(mb * TC_BM + lane_base);
+          if (p.batch > 1) tma_store_3d(&tmC, src, x, y, (int)bb);
+          else tma_store_2d(&tmC, src, x, y);
+          bulk_commit();
+        }
+      }
     }
+    if (tma_st && lane == 0) bulk_wait_all();
     if (p.check && __any_sync(0xffffffffu, bad) && bad) raise_flag(p.flags, FLAG_OVERFLOW, p.op_index);
   }
   tc_fence_before();

@@ -330,6 +330,7 @@ def run_ours(args):
             "roofline": roofline,
             "roofline_int8_gemm": gemm_roof,
             "kernel_us_by_kind": dict(sorted(by_kind.items(), key=lambda kv: -kv[1])),
+            "launch_us": [[d.label, C.KIND_NAMES[d.kind], round(u, 2)] for d, u in zip(prog.devops, kus)],
             "gpu_launches": sum(1 for d in prog.devops if d.kind != C.OP_COPY) * args.steps,
             "clocks": clk.summary()}
     if rank == 0 and ws == 1 and not args.no_sweep:
