@@ -557,9 +557,35 @@ static int launch_op(anvil_model *m, Launch &L) {
       const int dd = (int)op.dims[1];
       if (!chk && op.in_bytes == 1 && dd % 16 == 0 && dd <= 2048 && aligned16(L.ptr[0]) &&
           aligned16(L.ptr[1]) && aligned16(L.ptr[3]) && (!L.ptr[4] || aligned16(L.ptr[4]))) {
+        const int8_t *bias = (op.flags & ANVIL_F_BIAS) ? (const int8_t *)L.ptr[4] : nullptr;
+        if (dd % 256 == 0) {          // whole 8-byte vectors on every lane: the register-resident row kernel
+          // one resident wave: every warp then walks several rows with the next row's load in flight
+#define NR_LAUNCH(NV8)                                                                                            \
+  do {                                                                                                            \
+    static int per_sm = 0;                                                                                        \
+    if (!per_sm && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, norm_row_kernel<NV8>, 256, 0) != cudaSuccess) \
+      per_sm = 1;                                                                                                 \
+    const int g = grid_for(m, op.dims[0], 8, std::max(1, per_sm));                                                \
+    norm_row_kernel<NV8><<<g, 256, 0, st>>>((const int8_t *)L.ptr[0], (const int8_t *)L.ptr[1],                   \
+                                            (const int32_t *)L.ptr[2], bias, (int8_t *)L.ptr[3], op.dims[0],       \
+                                            (int)op.dims[2], (int)op.mult, (int)op.shift, (int)op.ss_shift,       \
+                                            (int)op.ss_init, (op.flags & ANVIL_F_CENTER) ? 1 : 0);                \
+  } while (0)
+          switch (dd / 256) {
+            case 1: NR_LAUNCH(1); break;
+            case 2: NR_LAUNCH(2); break;
+            case 3: NR_LAUNCH(3); break;
+            case 4: NR_LAUNCH(4); break;
+            case 5: NR_LAUNCH(5); break;
+            case 6: NR_LAUNCH(6); break;
+            case 7: NR_LAUNCH(7); break;
+            default: NR_LAUNCH(8); break;
+          }
+#undef NR_LAUNCH
+          break;
+        }
         const int nv = (dd / 16 + 31) / 32;
         const int g = grid_for(m, op.dims[0], 8, 16);
-        const int8_t *bias = (op.flags & ANVIL_F_BIAS) ? (const int8_t *)L.ptr[4] : nullptr;
 #define NV_LAUNCH(NV)                                                                                             \
   norm_vec_kernel<NV><<<g, 256, 0, st>>>((const int8_t *)L.ptr[0], (const int8_t *)L.ptr[1],                      \
                                          (const int32_t *)L.ptr[2], bias, (int8_t *)L.ptr[3], op.dims[0], dd,      \

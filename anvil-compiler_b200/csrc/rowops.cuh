@@ -260,6 +260,108 @@ __global__ void __launch_bounds__(256) norm_vec_kernel(const int8_t *__restrict_
   }
 }
 
+// Sign-extended byte q (0..3) of w in one byte permute: prmt's default mode replicates the sign bit of the
+// selected byte when the selector nibble's msb is set, so bytes 1-3 of the result copy the sign of byte q.
+__device__ __forceinline__ int sbyte_prmt(uint32_t w, int q) {
+  int r;
+  const uint32_t sel = (uint32_t)q | ((uint32_t)(q | 8) * 0x1110u);
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(sel));
+  return r;
+}
+
+// norm_vec for rows of d = 256 * NV8 int8 values (unchecked, static int32 proof). One warp per row, every lane
+// NV8 8-byte vectors (lane + 32 v); the weights and bias sign-extended into registers once per thread; the next
+// row's vectors loaded before the current row is computed (two rows in flight per warp). Row statistics come from
+// dp4a (sum and sum of squares, exact in int32 for d <= 2048); with no per-element shift (c == 0) the centered
+// sum of squares is sum(x^2) - 2 mean sum(x) + d mean^2, the same integer. The output multiplies (x - mean) * w by
+// r * M, equal mod 2^32 to ((x - mean) * w * r) * M, and exact because the proof bounds the true value.
+template <int NV8>
+__global__ void __launch_bounds__(256) norm_row_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w,
+                                                       const int32_t *__restrict__ lut,
+                                                       const int8_t *__restrict__ bias, int8_t *__restrict__ out,
+                                                       int64_t rows, int n, int m, int s, int c, int e, int center) {
+  constexpr int d = 256 * NV8;
+  const int lane = threadIdx.x & 31;
+  int wr[8 * NV8], br[8 * NV8];
+#pragma unroll
+  for (int v = 0; v < NV8; ++v) {
+    const uint2 w2 = reinterpret_cast<const uint2 *>(w)[lane + 32 * v];
+    const uint2 b2 = bias ? reinterpret_cast<const uint2 *>(bias)[lane + 32 * v] : make_uint2(0, 0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      wr[8 * v + q] = sbyte_prmt(q < 4 ? w2.x : w2.y, q & 3);
+      br[8 * v + q] = sbyte_prmt(q < 4 ? b2.x : b2.y, q & 3);
+    }
+  }
+  const int rc = c ? 1 << (c - 1) : 0;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  uint2 xv[NV8];
+  if (warp < rows) {
+#pragma unroll
+    for (int v = 0; v < NV8; ++v) xv[v] = reinterpret_cast<const uint2 *>(x + warp * d)[lane + 32 * v];
+  }
+  for (int64_t row = warp; row < rows; row += nwarps) {
+    uint2 xn[NV8];
+    const int64_t nrow = row + nwarps;
+    if (nrow < rows) {
+#pragma unroll
+      for (int v = 0; v < NV8; ++v) xn[v] = reinterpret_cast<const uint2 *>(x + nrow * d)[lane + 32 * v];
+    }
+    int sx = 0, sxx = 0;
+#pragma unroll
+    for (int v = 0; v < NV8; ++v) {
+      sx = __dp4a((int)xv[v].x, 0x01010101, sx);
+      sx = __dp4a((int)xv[v].y, 0x01010101, sx);
+      sxx = __dp4a((int)xv[v].x, (int)xv[v].x, sxx);
+      sxx = __dp4a((int)xv[v].y, (int)xv[v].y, sxx);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
+    int mean = 0;
+    if (center) {
+      const int num = sx + d / 2;                          // floor division by d > 0
+      mean = num >= 0 ? num / d : -((-num + d - 1) / d);
+    }
+    int ss;
+    if (c == 0) {
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sxx += __shfl_xor_sync(0xffffffffu, sxx, o);
+      ss = sxx - 2 * mean * sx + d * mean * mean;
+    } else {
+      ss = 0;
+#pragma unroll
+      for (int v = 0; v < NV8; ++v)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int xc = sbyte_prmt(q < 4 ? xv[v].x : xv[v].y, q & 3) - mean;
+          ss += (xc * xc + rc) >> c;
+        }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    }
+    ss += e;
+    int idx = ss, k = 0;
+    while (idx >= n) { idx >>= 2; ++k; }
+    const int rm = lut[idx] * m;
+    const int sh = s + k;
+    const int rnd = sh ? 1 << (sh - 1) : 0;
+    uint2 *orow = reinterpret_cast<uint2 *>(out + row * d);
+#pragma unroll
+    for (int v = 0; v < NV8; ++v) {
+      int y[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int xc = sbyte_prmt(q < 4 ? xv[v].x : xv[v].y, q & 3) - mean;
+        y[q] = (((xc * wr[8 * v + q]) * rm + rnd) >> sh) + br[8 * v + q];
+      }
+      orow[lane + 32 * v] = make_uint2(pack4_sat_s8(y[0], y[1], y[2], y[3]), pack4_sat_s8(y[4], y[5], y[6], y[7]));
+    }
+#pragma unroll
+    for (int v = 0; v < NV8; ++v) xv[v] = xn[v];
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ softmax
 // softmax_lut (anvil/lower/graph_to_tensor.py:352-398): one warp per row of (batch, T1, T2); kept j <= i when
 // causal; m = max(-128, x_j); e_j = lut[x_j - m + 255]; S = sum e_j; p_j = (e_j*one + S/2) / S (floor).

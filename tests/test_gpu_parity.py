@@ -184,6 +184,49 @@ def test_fused_attention_bit_exact(T, C, nh, causal, T2):
     _check(unfused.run([xb[s] for s in cm.inputs], "cuda", quantized=True).ints, want.values, cm.outputs)
 
 
+def _norm_case(seed, d, kind, with_bias, c):
+    from anvil.ir.graph import GraphBuilder
+    from graphs import mult_shift, rsqrt_lut
+    rng = np.random.default_rng(seed)
+    T = 300
+    g = GraphBuilder("norm")
+    consts = {"w": rng.integers(-128, 128, d), "rs": rsqrt_lut(1024)}
+    x = g.input("x", [T, d], "i8")
+    w = g.const("w", [d], "i8")
+    rs = g.const("rs", [1024], "i32")
+    # typical |(x - mean) w r / 2^k| is 40 * 64 * 2^15 / (50 sqrt(d)) (times 2^(c/2) with the ss shift): scale it
+    # to about 30 with M = 24, small enough that (x - mean) w r M stays inside int32
+    typ = 40 * 64 * (1 << 15) / (50 * np.sqrt(d)) * 2 ** (c / 2)
+    m, s = 24, int(round(np.log2(24 * typ / 30.0)))
+    e = int(rng.integers(0, 64)) if c else 0
+    if kind == "layernorm":
+        b = None
+        if with_bias:
+            consts["b"] = rng.integers(-20, 21, d)
+            b = g.const("b", [d], "i8")
+        y = g.layernorm_int("y", x, w, rs, m, s, ss_shift=c, ss_init=e, bias=b)
+    else:
+        y = g.rmsnorm_int("y", x, w, rs, m, s, ss_shift=c, ss_init=e)
+    g.output(y)
+    xs = np.clip(np.rint(rng.normal(float(rng.integers(-30, 31)), 50.0, (2, T, d))), -128, 127).astype(np.int64)
+    xs[0, 0] = 127                                   # saturated rows
+    xs[0, 1] = -128
+    return g.module(), {k: np.asarray(v, dtype=np.int64) for k, v in consts.items()}, xs
+
+
+@pytest.mark.parametrize("d", [256, 768, 2048])
+@pytest.mark.parametrize("kind,with_bias,c", [("layernorm", True, 0), ("layernorm", False, 0), ("rmsnorm", False, 0),
+                                              ("layernorm", True, 3), ("rmsnorm", False, 2)])
+@pytest.mark.parametrize("checked", [False, True])
+def test_norm_rows_bit_exact(d, kind, with_bias, c, checked):
+    """LayerNorm / RMSNorm rows of i8 (the register-resident row kernel for d a multiple of 256 when unchecked, the
+    general row kernel when checked) vs the oracle, 2 x 300 rows with a per-row offset, saturated rows included."""
+    module, consts, xs = _norm_case(d * 7 + c, d, kind, with_bias, c)
+    want = interp.run(module, {"x": xs}, consts, batch=True)
+    cm = anvil.compile(module, consts=consts, prove=False, params=CudaParams(checked=checked))
+    _check(cm.run(xs, "cuda", quantized=True).ints, want.values, cm.outputs)
+
+
 def test_c3_block_fused_matches_oracle():
     """Config c3 (GPT-2-small int8 block, T 1024) through the torch frontend: 2 sequences on the GPU vs the oracle."""
     from anvil import workloads as W
