@@ -642,8 +642,9 @@ static int launch_op(anvil_model *m, Launch &L) {
       break;
     case ANVIL_OP_ATTENTION: {
       const AttnParams &a = L.ap;
-      const int64_t grid = (int64_t)a.B * a.H * a.nqt;
-      if (grid > 0x7fffffff) return fail(ANVIL_E_BAD_ARG, "op %d: attention grid too large", oi);
+      const int64_t tiles = (int64_t)a.B * a.H * a.nqt;      // persistent: one CTA per SM walks the tiles
+      if (tiles > 0x7fffffff) return fail(ANVIL_E_BAD_ARG, "op %d: attention has too many tiles", oi);
+      const int64_t grid = std::min<int64_t>(tiles, m->sms);
       if (L.hd == 64)
         attn_kernel<64><<<(unsigned)grid, ATTN_THREADS, AttnCfg<64>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, a);
       else

@@ -3,10 +3,13 @@
 //   p      = softmax_lut(scores, exp_lut, one, causal)                  (anvil/lower/graph_to_tensor.py:352-398)
 //   o      = requant(p @ v, M2, s2), written straight into the merged-heads layout (b, t, h*hd + d)
 //
-// One CTA per (batch, head, 128-query tile), heaviest causal tiles first. Warp roles:
-//   warp 0     TMA: the Q tile once, then through one NS-deep ring the K tiles (128 keys x hd) and after them
-//              the V^T slabs (hd x 128 keys, from the head-major transposed V the v-projection GEMM writes), so the
-//              V loads land while the softmax runs
+// Persistent: one CTA per SM walks the (batch, head, 128-query tile) work items, heaviest causal tiles first, in a
+// boustrophedon order over the CTAs. The exp LUT, the TMEM allocation and the barriers are set up once per CTA,
+// and the next tile's first two score MMAs run while the softmax warps finish the current tile. Warp roles:
+//   warp 0     TMA: per tile the Q tile (one buffer, reloaded once the tile's score MMAs are done) and the K tiles
+//              (128 keys x hd) through a KS-deep ring
+//   warp 18    TMA: the V^T slabs (hd x 128 keys, from the head-major transposed V the v-projection GEMM writes)
+//              through a VS-deep ring, so they land while the softmax runs
 //   warp 1     tcgen05.mma kind::i8: S_j = Q K_j^T into one of two TMEM buffers (128 x 128 int32); after the
 //              softmax, O = sum_j P_j V_j into a third TMEM region (128 x hd)
 //   warps 2-17 four threads per query row, each owning a 32-column part of every 128-key slab: drain S_j from
@@ -37,19 +40,21 @@ struct AttnParams {
 
 template <int HD>
 struct AttnCfg {
-  static constexpr int NS = HD == 64 ? 6 : 4;           // one ring for K tiles then V^T slabs (same size)
+  static constexpr int KS = HD == 64 ? 3 : 2;            // K-tile ring slots
+  static constexpr int VS = HD == 64 ? 3 : 2;            // V^T-slab ring slots
   static constexpr int LUT_COPIES = HD == 64 ? 32 : 8;  // exp LUT replicated per lane: conflict-free lookups
   static constexpr int Q_BYTES = 128 * HD;
   static constexpr int T_BYTES = 128 * HD;              // a K tile (128 keys x hd) or a V^T slab (hd x 128 keys)
   static constexpr int MAX_SLABS = 8;                   // T2 <= 1024
   static constexpr int P_SLAB = 128 * 128;
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_R = OFF_Q + Q_BYTES;
-  static constexpr int OFF_P = OFF_R + NS * T_BYTES;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_V = OFF_K + KS * T_BYTES;
+  static constexpr int OFF_P = OFF_V + VS * T_BYTES;
   static constexpr int OFF_LUT = OFF_P + MAX_SLABS * P_SLAB;
-  static constexpr int OFF_RED = OFF_LUT + 1024 * LUT_COPIES;       // [4][128] int32 row partials
-  static constexpr int OFF_BAR = OFF_RED + 2048;
-  static constexpr int NBAR = 1 + 2 * NS + 2 + 2 + 1 + 1;
+  static constexpr int OFF_RED = OFF_LUT + 1024 * LUT_COPIES;       // [2][4][128] int32: row max, row sum partials
+  static constexpr int OFF_BAR = OFF_RED + 4096;
+  static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 4 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   // Q / K tiles: rows of HD bytes. 64-byte rows use the 64-byte swizzle (8-row atoms of 512 B), 128-byte rows
@@ -90,7 +95,33 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
 __device__ __forceinline__ int pslab_off(int r, int ch) { return (r >> 3) * 1024 + (r & 7) * 128 + ((ch ^ (r & 7)) << 4); }
 
 constexpr int ATTN_SOFTMAX_THREADS = 512;                 // 16 warps: 4 threads per query row
-constexpr int ATTN_THREADS = 64 + ATTN_SOFTMAX_THREADS;
+constexpr int ATTN_THREADS = 64 + ATTN_SOFTMAX_THREADS + 32;   // + warp 18, the V^T producer
+
+// One work item: (batch, head) and a 128-query tile, heaviest causal tiles first.
+struct AttnTile {
+  int b, h, bh, q0, nkv;
+};
+
+__device__ __forceinline__ AttnTile attn_tile(const AttnParams &p, int t) {
+  const int BH = p.B * p.H;
+  AttnTile w;
+  const int qt = p.nqt - 1 - t / BH;
+  w.bh = t % BH;
+  w.b = w.bh / p.H;
+  w.h = w.bh % p.H;
+  w.q0 = qt * 128;
+  const int kv_end = p.causal ? min(p.T2, w.q0 + 128) : p.T2;
+  w.nkv = (kv_end + 127) / 128;
+  return w;
+}
+
+// The k-th work item of this CTA: rounds of gridDim.x items, alternating direction (boustrophedon), so the CTAs
+// that take the heavier end of one round take the lighter end of the next. -1 past the end.
+__device__ __forceinline__ int attn_item(int k, int ntiles) {
+  const int g = (int)gridDim.x, c = (int)blockIdx.x;
+  const int t = k * g + ((k & 1) ? g - 1 - c : c);
+  return t < ntiles ? t : -1;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(ATTN_THREADS, 1)
@@ -100,27 +131,23 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align_smem_1024(smem_raw);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::OFF_BAR);
-  uint64_t *qfull = bars;
-  uint64_t *rfull = qfull + 1, *rempty = rfull + Cfg::NS;
-  uint64_t *sfull = rempty + Cfg::NS, *sempty = sfull + 2;
+  uint64_t *qfull = bars, *qempty = bars + 1;
+  uint64_t *kfull = bars + 2, *kempty = kfull + Cfg::KS;
+  uint64_t *vfull = kempty + Cfg::KS, *vempty = vfull + Cfg::VS;
+  uint64_t *sfull = vempty + Cfg::VS, *sempty = sfull + 2;
   uint64_t *pready = sempty + 2, *ofull = pready + 1;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Cfg::OFF_MISC);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + Cfg::OFF_MISC + 4);
   int32_t *lut = reinterpret_cast<int32_t *>(smem + Cfg::OFF_LUT);   // entry i of copy c at word i*COPIES + c
   uint8_t *pbuf = smem + Cfg::OFF_P;
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int BH = p.B * p.H;
-  const int qt = p.nqt - 1 - (int)(blockIdx.x / BH);
-  const int bh = (int)(blockIdx.x % BH);
-  const int b = bh / p.H, h = bh % p.H;
-  const int q0 = qt * 128;
-  const int kv_end = p.causal ? min(p.T2, q0 + 128) : p.T2;
-  const int nkv = (kv_end + 127) / 128;
+  const int ntiles = p.B * p.H * p.nqt;
 
   if (threadIdx.x == 0) {
     mbar_init(qfull, 1);
-    for (int i = 0; i < Cfg::NS; ++i) { mbar_init(&rfull[i], 1); mbar_init(&rempty[i], 1); }
+    mbar_init(qempty, 1);
+    for (int i = 0; i < Cfg::KS; ++i) { mbar_init(&kfull[i], 1); mbar_init(&kempty[i], 1); }
+    for (int i = 0; i < Cfg::VS; ++i) { mbar_init(&vfull[i], 1); mbar_init(&vempty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&sfull[i], 1); mbar_init(&sempty[i], ATTN_SOFTMAX_THREADS); }
     mbar_init(pready, ATTN_SOFTMAX_THREADS);
     mbar_init(ofull, 1);
@@ -138,214 +165,286 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
+    // ------------------------------------------------------------------ TMA: Q and the K tiles
     if (elect_one()) {
       prefetch_tmap(&mapQ);
       prefetch_tmap(&mapK);
-      prefetch_tmap(&mapV);
       bool ok = true;
-      mbar_arrive_expect_tx(qfull, Cfg::Q_BYTES);
-      tma_load_4d(smem + Cfg::OFF_Q, &mapQ, 0, h, q0, b, qfull);
-      // ring sequence g: K tiles 0..nkv-1, then V^T slabs 0..nkv-1 (the V loads land while the softmax runs)
-      for (int g = 0; g < 2 * nkv && ok; ++g) {
-        const int st = g % Cfg::NS;
-        if (!mbar_wait_idle(&rempty[st], ((g / Cfg::NS) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
-        mbar_arrive_expect_tx(&rfull[st], Cfg::T_BYTES);
-        uint8_t *dst = smem + Cfg::OFF_R + st * Cfg::T_BYTES;
-        if (g < nkv) tma_load_4d(dst, &mapK, 0, h, g * 128, b, &rfull[st]);
-        else tma_load_2d(dst, &mapV, (g - nkv) * 128, bh * HD, &rfull[st]);
+      uint32_t gk = 0;
+      for (int k = 0, t; ok && (t = attn_item(k, ntiles)) >= 0; ++k) {
+        const AttnTile w = attn_tile(p, t);
+        if (!mbar_wait_idle(qempty, (k & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
+        mbar_arrive_expect_tx(qfull, Cfg::Q_BYTES);
+        tma_load_4d(smem + Cfg::OFF_Q, &mapQ, 0, w.h, w.q0, w.b, qfull);
+        for (int j = 0; j < w.nkv; ++j, ++gk) {
+          const int st = gk % Cfg::KS;
+          if (!mbar_wait_idle(&kempty[st], ((gk / Cfg::KS) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kfull[st], Cfg::T_BYTES);
+          tma_load_4d(smem + Cfg::OFF_K + st * Cfg::T_BYTES, &mapK, 0, w.h, j * 128, w.b, &kfull[st]);
+        }
       }
       if (!ok) {              // aborted: let the copies already issued land before the CTA exits
         mbar_wait_ns(qfull, 0, 10000000ull);
-        for (int s2 = 0; s2 < Cfg::NS; ++s2) {
-          mbar_wait_ns(&rfull[s2], 0, 10000000ull);
-          mbar_wait_ns(&rfull[s2], 1, 10000000ull);
+        mbar_wait_ns(qfull, 1, 10000000ull);
+        for (int s2 = 0; s2 < Cfg::KS; ++s2) {
+          mbar_wait_ns(&kfull[s2], 0, 10000000ull);
+          mbar_wait_ns(&kfull[s2], 1, 10000000ull);
+        }
+      }
+    }
+  } else if (warp == 2 + ATTN_SOFTMAX_THREADS / 32) {
+    // ------------------------------------------------------------------ TMA: the V^T slabs
+    if (elect_one()) {
+      prefetch_tmap(&mapV);
+      bool ok = true;
+      uint32_t gv = 0;
+      for (int k = 0, t; ok && (t = attn_item(k, ntiles)) >= 0; ++k) {
+        const AttnTile w = attn_tile(p, t);
+        for (int j = 0; j < w.nkv; ++j, ++gv) {
+          const int st = gv % Cfg::VS;
+          if (!mbar_wait_idle(&vempty[st], ((gv / Cfg::VS) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
+          mbar_arrive_expect_tx(&vfull[st], Cfg::T_BYTES);
+          tma_load_2d(smem + Cfg::OFF_V + st * Cfg::T_BYTES, &mapV, j * 128, w.bh * HD, &vfull[st]);
+        }
+      }
+      if (!ok) {
+        for (int s2 = 0; s2 < Cfg::VS; ++s2) {
+          mbar_wait_ns(&vfull[s2], 0, 10000000ull);
+          mbar_wait_ns(&vfull[s2], 1, 10000000ull);
         }
       }
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       constexpr uint32_t idesc_qk = idesc_i8(128, 128);
       constexpr uint32_t idesc_pv = idesc_i8(128, HD);
       const uint32_t sq = smem_u32(smem + Cfg::OFF_Q);
-      bool ok = mbar_wait(qfull, 0, abort, p.flags, p.op_index);
-      tc_fence_after();
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int sb = j & 1, st = j % Cfg::NS;
-        if (!mbar_wait(&sempty[sb], ((j >> 1) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
-        if (!mbar_wait(&rfull[st], (j / Cfg::NS) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
+      uint32_t gk = 0, gv = 0, gs = 0;
+      // S = Q K_j^T for the next K tile into the next S buffer (the tile's Q is resident)
+      auto issue_s = [&]() -> bool {
+        const int sb = gs & 1, st = gk % Cfg::KS;
+        if (!mbar_wait(&sempty[sb], ((gs >> 1) & 1) ^ 1, abort, p.flags, p.op_index)) return false;
+        if (!mbar_wait(&kfull[st], (gk / Cfg::KS) & 1, abort, p.flags, p.op_index)) return false;
         tc_fence_after();
-        const uint32_t sk = smem_u32(smem + Cfg::OFF_R + st * Cfg::T_BYTES);
+        const uint32_t sk = smem_u32(smem + Cfg::OFF_K + st * Cfg::T_BYTES);
 #pragma unroll
         for (int kk = 0; kk < HD / 32; ++kk)
           mma_i8(tmem + sb * 128, kmajor_desc(sq + 32 * kk, Cfg::QK_LAYOUT, Cfg::QK_SBO),
                  kmajor_desc(sk + 32 * kk, Cfg::QK_LAYOUT, Cfg::QK_SBO), idesc_qk, kk > 0 ? 1u : 0u);
-        mma_commit(&rempty[st]);
+        mma_commit(&kempty[st]);
         mma_commit(&sfull[sb]);
-      }
-      if (ok) ok = mbar_wait_idle(pready, 0, abort, p.flags, p.op_index);
-      tc_fence_after();
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int g = nkv + j, st = g % Cfg::NS;
-        if (!mbar_wait(&rfull[st], (g / Cfg::NS) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
+        ++gk;
+        ++gs;
+        return true;
+      };
+      bool ok = true;
+      int t = attn_item(0, ntiles);
+      if (t >= 0) {                     // the first tile's first two score MMAs
+        const AttnTile w = attn_tile(p, t);
+        ok = mbar_wait(qfull, 0, abort, p.flags, p.op_index);
         tc_fence_after();
-        const uint32_t sp = smem_u32(pbuf + j * Cfg::P_SLAB);
-        const uint32_t sv = smem_u32(smem + Cfg::OFF_R + st * Cfg::T_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_i8(tmem + 256, kmajor_desc(sp + 32 * kk, 2u, 1024u), kmajor_desc(sv + 32 * kk, 2u, 1024u), idesc_pv,
-                 (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&rempty[st]);
+        for (int j = 0; ok && j < min(2, w.nkv); ++j) ok = issue_s();
       }
-      if (ok) mma_commit(ofull);
+      for (int k = 0; ok && t >= 0; ++k) {
+        const AttnTile w = attn_tile(p, t);
+        for (int j = 2; ok && j < w.nkv; ++j) ok = issue_s();
+        if (!ok) break;
+        mma_commit(qempty);             // the Q buffer is free once this tile's score MMAs are done
+        // the next tile's first two score MMAs overlap this tile's softmax passes
+        const int tn = attn_item(k + 1, ntiles);
+        if (tn >= 0) {
+          const AttnTile wn = attn_tile(p, tn);
+          if (!mbar_wait_idle(qfull, (k + 1) & 1, abort, p.flags, p.op_index)) break;
+          tc_fence_after();
+          for (int j = 0; ok && j < min(2, wn.nkv); ++j) ok = issue_s();
+          if (!ok) break;
+        }
+        if (!mbar_wait_idle(pready, k & 1, abort, p.flags, p.op_index)) break;
+        tc_fence_after();
+        for (int j = 0; ok && j < w.nkv; ++j, ++gv) {
+          const int st = gv % Cfg::VS;
+          if (!mbar_wait(&vfull[st], (gv / Cfg::VS) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sp = smem_u32(pbuf + j * Cfg::P_SLAB);
+          const uint32_t sv = smem_u32(smem + Cfg::OFF_V + st * Cfg::T_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_i8(tmem + 256, kmajor_desc(sp + 32 * kk, 2u, 1024u), kmajor_desc(sv + 32 * kk, 2u, 1024u),
+                   idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&vempty[st]);
+        }
+        if (!ok) break;
+        mma_commit(ofull);
+        t = tn;
+      }
     }
   } else {
     // -------------------------------------------- softmax warps: 4 threads per query row, one 32-column part each
     const int lane_base = 32 * (warp & 3);           // TMEM lanes this warp may read
     const int part = (warp - 2) >> 2;                // 0..3: columns [32*part, 32*part + 32) of every slab
     const int r = lane_base + lane;
-    const int row = q0 + r;
-    const int kept = p.causal ? min(row + 1, p.T2) : p.T2;
     const int m1 = (int)p.m1;
     const int rnd1 = (int)round_term(p.s1);
-    int32_t *red = reinterpret_cast<int32_t *>(smem + Cfg::OFF_RED);   // [4][128] partial max / sum per row
+    int32_t *red_max = reinterpret_cast<int32_t *>(smem + Cfg::OFF_RED);   // [4][128] partial row max
+    int32_t *red_sum = red_max + 512;                                          // [4][128] partial row sum
     const int lcopy = lane % Cfg::LUT_COPIES;
-    int mx = -128;
-    bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      const int sb = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait_idle(&sfull[sb], (j >> 1) & 1, abort, p.flags, p.op_index));
-      if (!ok) break;                       // warp-uniform: the TMEM load below is .sync.aligned
-      tc_fence_after();
-      int32_t acc[32];
-      tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(sb * 128 + part * 32), acc);
-      uint32_t w[8];
-      const int cbase = j * 128 + part * 32;
-      // the static int32 proof holds on this path: acc*M1 + 2^(s1-1) fits int32. The row max is taken over the
-      // unclamped values (clamping is monotone, so max of clamped = clamp of max) and the clamp happens in the
-      // saturating pack.
-      int v[32];
+    const long long rnd2 = round_term(p.s2);
+    uint32_t gs = 0;
+    for (int k = 0, t; (t = attn_item(k, ntiles)) >= 0; ++k) {
+      // every softmax warp takes the same decision to stop (the named barriers below need all 16): the abort word
+      // is OR-reduced across the 512 threads by the barrier itself
+      int stop;
+      asm volatile(
+          "{\n\t.reg .pred P;\n\t"
+          "setp.ne.s32 P, %1, 0;\n\t"
+          "bar.red.or.pred P, 1, 512, P;\n\t"
+          "selp.s32 %0, 1, 0, P;\n\t}"
+          : "=r"(stop)
+          : "r"(*abort)
+          : "memory");
+      if (stop) break;
+      const AttnTile w = attn_tile(p, t);
+      const int row = w.q0 + r;
+      const int kept = p.causal ? min(row + 1, p.T2) : p.T2;
+      int mx = -128;
+      bool ok = true;
+      for (int j = 0; j < w.nkv; ++j, ++gs) {
+        const int sb = gs & 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&sfull[sb], (gs >> 1) & 1, abort, p.flags, p.op_index));
+        if (!ok) break;                     // warp-uniform: the TMEM load below is .sync.aligned
+        tc_fence_after();
+        int32_t acc[32];
+        tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(sb * 128 + part * 32), acc);
+        uint32_t wq[8];
+        const int cbase = j * 128 + part * 32;
+        // the static int32 proof holds on this path: acc*M1 + 2^(s1-1) fits int32. The row max is taken over the
+        // unclamped values (clamping is monotone, so max of clamped = clamp of max) and the clamp happens in the
+        // saturating pack.
+        int v[32];
 #pragma unroll
-      for (int q = 0; q < 32; ++q) v[q] = (acc[q] * m1 + rnd1) >> p.s1;
-      if (cbase + 32 <= kept) {             // every column of this part is kept: no mask test
+        for (int q = 0; q < 32; ++q) v[q] = (acc[q] * m1 + rnd1) >> p.s1;
+        if (cbase + 32 <= kept) {           // every column of this part is kept: no mask test
 #pragma unroll
-        for (int q = 0; q < 32; ++q) mx = max(mx, v[q]);
-      } else {
+          for (int q = 0; q < 32; ++q) mx = max(mx, v[q]);
+        } else {
 #pragma unroll
-        for (int q = 0; q < 32; ++q)
-          if (cbase + q < kept) mx = max(mx, v[q]);
+          for (int q = 0; q < 32; ++q)
+            if (cbase + q < kept) mx = max(mx, v[q]);
+        }
+        // the slab holds each score biased by 128 (x + 128 as an unsigned byte), so both passes below read it
+        // with one zero-extending byte extract; pass B overwrites it with the probabilities
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          wq[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]) ^ 0x80808080u;
+        uint8_t *slab = pbuf + j * Cfg::P_SLAB;
+        *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part)) = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+        *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part + 1)) = make_uint4(wq[4], wq[5], wq[6], wq[7]);
+        tc_fence_before();
+        mbar_arrive(&sempty[sb]);
       }
-      // the slab holds each score biased by 128 (x + 128 as an unsigned byte), so both passes below read it
-      // with one zero-extending byte extract; pass B overwrites it with the probabilities
+      // row max over the 4 parts (clamped: the raw scores were tracked). The max and the sum have their own
+      // partial arrays, so a warp that runs ahead into the next tile cannot overwrite what a slower one still reads.
+      red_max[part * 128 + r] = min(127, mx);
+      asm volatile("bar.sync 1, 512;" ::: "memory");
+      mx = max(max(red_max[r], red_max[128 + r]), max(red_max[256 + r], red_max[384 + r]));
+      // a kept score x <= mx is stored as u = x + 128, and lut[x - mx + 255] = lut[u + 127 - mx]: lutc[u * COPIES]
+      // is that entry in this lane's copy (index 0..255 for every kept u)
+      const int32_t *lutc = lut + (127 - mx) * Cfg::LUT_COPIES + lcopy;
+      // pass A: partial S = sum over this part's kept columns of lut[x - max + 255]
+      int tot0 = 0, tot1 = 0;
+      for (int j = 0; j < w.nkv && ok; ++j) {
+        const uint8_t *slab = pbuf + j * Cfg::P_SLAB;
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]) ^ 0x80808080u;
-      uint8_t *slab = pbuf + j * Cfg::P_SLAB;
-      *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part)) = make_uint4(w[0], w[1], w[2], w[3]);
-      *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
-      tc_fence_before();
-      mbar_arrive(&sempty[sb]);
-    }
-    // row max over the 4 parts (clamped: the raw scores were tracked)
-    red[part * 128 + r] = min(127, mx);
-    asm volatile("bar.sync 1, 512;" ::: "memory");
-    mx = max(max(red[r], red[128 + r]), max(red[256 + r], red[384 + r]));
-    asm volatile("bar.sync 1, 512;" ::: "memory");
-    // a kept score x <= mx is stored as u = x + 128, and lut[x - mx + 255] = lut[u + 127 - mx]: lutc[u * COPIES]
-    // is that entry in this lane's copy (index 0..255 for every kept u)
-    const int32_t *lutc = lut + (127 - mx) * Cfg::LUT_COPIES + lcopy;
-    // pass A: partial S = sum over this part's kept columns of lut[x - max + 255]
-    int tot0 = 0, tot1 = 0;
-    for (int j = 0; j < nkv && ok; ++j) {
-      const uint8_t *slab = pbuf + j * Cfg::P_SLAB;
+        for (int hh = 0; hh < 2; ++hh) {
+          const int c0 = j * 128 + part * 32 + hh * 16;
+          if (c0 < kept) {
+            const uint4 v4 = *reinterpret_cast<const uint4 *>(slab + pslab_off(r, 2 * part + hh));
+            const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
+            if (c0 + 16 <= kept) {
+              // two independent three-input adds per word (each folds two entries into one accumulator)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int c0 = j * 128 + part * 32 + hh * 16;
-        if (c0 < kept) {
-          const uint4 v4 = *reinterpret_cast<const uint4 *>(slab + pslab_off(r, 2 * part + hh));
-          const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
-          if (c0 + 16 <= kept) {
-            // two independent three-input adds per word (each folds two entries into one accumulator)
+              for (int q = 0; q < 4; ++q) {
+                tot0 += lutc[ubyte(wv[q], 0) * Cfg::LUT_COPIES] + lutc[ubyte(wv[q], 1) * Cfg::LUT_COPIES];
+                tot1 += lutc[ubyte(wv[q], 2) * Cfg::LUT_COPIES] + lutc[ubyte(wv[q], 3) * Cfg::LUT_COPIES];
+              }
+            } else {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              tot0 += lutc[ubyte(wv[q], 0) * Cfg::LUT_COPIES] + lutc[ubyte(wv[q], 1) * Cfg::LUT_COPIES];
-              tot1 += lutc[ubyte(wv[q], 2) * Cfg::LUT_COPIES] + lutc[ubyte(wv[q], 3) * Cfg::LUT_COPIES];
+              for (int q = 0; q < 16; ++q) {
+                if (c0 + q < kept) tot0 += lutc[ubyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES];
+              }
             }
-          } else {
+          }
+        }
+      }
+      red_sum[part * 128 + r] = tot0 + tot1;
+      asm volatile("bar.sync 1, 512;" ::: "memory");
+      const int tot = red_sum[r] + red_sum[128 + r] + red_sum[256 + r] + red_sum[384 + r];
+      // pass B: p = floor((e*one + S/2) / S), masked entries 0. The division is a multiply by a per-row magic
+      // number (Granlund & Montgomery, "Division by invariant integers using multiplication", 1994): with
+      // l = ceil(log2 S), k = 31 + l and m = ceil(2^k / S) (m <= 2^32), floor(n m / 2^k) = floor(n / S) for every
+      // 0 <= n < 2^31, because m S - 2^k < S <= 2^l makes the error term n (m S - 2^k) / (S 2^k) < 1 / S.
+      // With m < 2^32 this is a 32 x 32 -> high 32 multiply and a shift by l - 1. S = 1 takes the same form with
+      // n doubled (one2 = 2*one, m = 2^31, shift 0): the high word of 2n * 2^31 is n (2n < 2^32 as e*one < 2^31).
+      const int S = tot > 0 ? tot : 1;
+      const int lg = S > 1 ? 32 - __clz(S - 1) : 0;
+      const unsigned magic =
+          S > 1 ? (unsigned)(((1ull << (31 + lg)) + (unsigned long long)(S - 1)) / (unsigned long long)S) : 0x80000000u;
+      const int msh = lg > 0 ? lg - 1 : 0;
+      const unsigned one2 = S > 1 ? (unsigned)p.one : 2u * (unsigned)p.one;
+      const unsigned half2 = S > 1 ? (unsigned)(tot >> 1) : 2u * (unsigned)(tot >> 1);
+      for (int j = 0; j < w.nkv && ok; ++j) {
+        uint8_t *slab = pbuf + j * Cfg::P_SLAB;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int c0 = j * 128 + part * 32 + hh * 16;
+          const int off = pslab_off(r, 2 * part + hh);
+          uint4 v4 = *reinterpret_cast<const uint4 *>(slab + off);
+          const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
+          uint32_t ov[4] = {0, 0, 0, 0};
+          if (c0 + 16 <= kept) {
+            int pv[16];
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
-              if (c0 + q < kept) tot0 += lutc[ubyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES];
-            }
-          }
-        }
-      }
-    }
-    red[part * 128 + r] = tot0 + tot1;
-    asm volatile("bar.sync 1, 512;" ::: "memory");
-    const int tot = red[r] + red[128 + r] + red[256 + r] + red[384 + r];
-    // pass B: p = floor((e*one + S/2) / S), masked entries 0. The division is a multiply by a per-row magic
-    // number (Granlund & Montgomery, "Division by invariant integers using multiplication", 1994): with
-    // l = ceil(log2 S), k = 31 + l and m = ceil(2^k / S) (m <= 2^32), floor(n m / 2^k) = floor(n / S) for every
-    // 0 <= n < 2^31, because m S - 2^k < S <= 2^l makes the error term n (m S - 2^k) / (S 2^k) < 1 / S.
-    // With m < 2^32 this is a 32 x 32 -> high 32 multiply and a shift by l - 1. S = 1 takes the same form with
-    // n doubled (one2 = 2*one, m = 2^31, shift 0): the high word of 2n * 2^31 is n (2n < 2^32 as e*one < 2^31).
-    const int S = tot > 0 ? tot : 1;
-    const int lg = S > 1 ? 32 - __clz(S - 1) : 0;
-    const unsigned magic =
-        S > 1 ? (unsigned)(((1ull << (31 + lg)) + (unsigned long long)(S - 1)) / (unsigned long long)S) : 0x80000000u;
-    const int msh = lg > 0 ? lg - 1 : 0;
-    const unsigned one2 = S > 1 ? (unsigned)p.one : 2u * (unsigned)p.one;
-    const unsigned half2 = S > 1 ? (unsigned)(tot >> 1) : 2u * (unsigned)(tot >> 1);
-    for (int j = 0; j < nkv && ok; ++j) {
-      uint8_t *slab = pbuf + j * Cfg::P_SLAB;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int c0 = j * 128 + part * 32 + hh * 16;
-        const int off = pslab_off(r, 2 * part + hh);
-        uint4 v4 = *reinterpret_cast<const uint4 *>(slab + off);
-        const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
-        uint32_t ov[4] = {0, 0, 0, 0};
-        if (c0 + 16 <= kept) {
-          int pv[16];
-#pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            const unsigned num = (unsigned)lutc[ubyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES] * one2 + half2;
-            pv[q] = (int)(__umulhi(num, magic) >> msh);
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q) ov[q] = pack4_sat_s8(pv[4 * q], pv[4 * q + 1], pv[4 * q + 2], pv[4 * q + 3]);
-        } else if (c0 < kept) {
-#pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            unsigned pq = 0;
-            if (c0 + q < kept) {
               const unsigned num = (unsigned)lutc[ubyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES] * one2 + half2;
-              pq = __umulhi(num, magic) >> msh;
+              pv[q] = (int)(__umulhi(num, magic) >> msh);
             }
-            ov[q >> 2] |= (pq & 0xffu) << (8 * (q & 3));
+#pragma unroll
+            for (int q = 0; q < 4; ++q) ov[q] = pack4_sat_s8(pv[4 * q], pv[4 * q + 1], pv[4 * q + 2], pv[4 * q + 3]);
+          } else if (c0 < kept) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              unsigned pq = 0;
+              if (c0 + q < kept) {
+                const unsigned num = (unsigned)lutc[ubyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES] * one2 + half2;
+                pq = __umulhi(num, magic) >> msh;
+              }
+              ov[q >> 2] |= (pq & 0xffu) << (8 * (q & 3));
+            }
           }
+          *reinterpret_cast<uint4 *>(slab + off) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
         }
-        *reinterpret_cast<uint4 *>(slab + off) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
       }
-    }
-    fence_proxy_async();
-    mbar_arrive(pready);
-    // O = P V from TMEM -> requant -> merged-heads output row (parts 0 .. HD/32-1 take 32 columns each)
-    if (ok && part < HD / 32 && __all_sync(0xffffffffu, mbar_wait_idle(ofull, 0, abort, p.flags, p.op_index))) {
-      tc_fence_after();
-      const long long rnd2 = round_term(p.s2);
-      int32_t acc[32];
-      tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(256 + part * 32), acc);
-      uint32_t w[8];
-      int v[32];
+      fence_proxy_async();
+      mbar_arrive(pready);
+      // O = P V from TMEM -> requant -> merged-heads output row (parts 0 .. HD/32-1 take 32 columns each)
+      if (ok && part < HD / 32 && __all_sync(0xffffffffu, mbar_wait(ofull, k & 1, abort, p.flags, p.op_index))) {
+        tc_fence_after();
+        int32_t acc[32];
+        tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(256 + part * 32), acc);
+        uint32_t wq[8];
+        int v[32];
 #pragma unroll
-      for (int q = 0; q < 32; ++q) v[q] = (int)clampi(((long long)acc[q] * p.m2 + rnd2) >> p.s2, -128, 127);
+        for (int q = 0; q < 32; ++q) v[q] = (int)clampi(((long long)acc[q] * p.m2 + rnd2) >> p.s2, -128, 127);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-      if (row < p.T1) {
-        int8_t *orow = p.out + (int64_t)b * p.o_bs + (int64_t)row * p.o_rs + (int64_t)h * HD + part * 32;
-        uint4 *d4 = reinterpret_cast<uint4 *>(orow);
-        d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        for (int q = 0; q < 8; ++q) wq[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        if (row < p.T1) {
+          int8_t *orow = p.out + (int64_t)w.b * p.o_bs + (int64_t)row * p.o_rs + (int64_t)w.h * HD + part * 32;
+          uint4 *d4 = reinterpret_cast<uint4 *>(orow);
+          d4[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+          d4[1] = make_uint4(wq[4], wq[5], wq[6], wq[7]);
+        }
+        tc_fence_before();
       }
     }
   }
