@@ -4,20 +4,21 @@
 //   o      = requant(p @ v, M2, s2), written straight into the merged-heads layout (b, t, h*hd + d)
 //
 // Persistent: one CTA per SM walks the (batch, head, 128-query tile) work items, heaviest causal tiles first, in a
-// boustrophedon order over the CTAs. The exp LUT, the TMEM allocation and the barriers are set up once per CTA,
-// and the next tile's first two score MMAs run while the softmax warps finish the current tile. Warp roles:
+// boustrophedon order over the CTAs. The exp LUT, the TMEM allocation and the barriers are set up once per CTA.
+// Warp roles:
 //   warp 0     TMA: per tile the Q tile (one buffer, reloaded once the tile's score MMAs are done) and the K tiles
 //              (128 keys x hd) through a KS-deep ring
 //   warp 18    TMA: the V^T slabs (hd x 128 keys, from the head-major transposed V the v-projection GEMM writes)
-//              through a VS-deep ring, so they land while the softmax runs
-//   warp 1     tcgen05.mma kind::i8: S_j = Q K_j^T into one of two TMEM buffers (128 x 128 int32); after the
-//              softmax, O = sum_j P_j V_j into a third TMEM region (128 x hd)
+//              through a VS-deep ring
+//   warp 1     tcgen05.mma kind::i8: S_j = Q K_j^T into one of NSB TMEM score buffers (128 x 128 int32 each); the
+//              next tile's first NSB score MMAs are issued before this tile's P V MMAs; O = sum_j P_j V_j slab by
+//              slab as the softmax warps finish each slab's probabilities, into a separate TMEM region (128 x hd)
 //   warps 2-17 four threads per query row, each owning a 32-column part of every 128-key slab: drain S_j from
 //              TMEM, requant to int8, track the partial row max, store into the P slab j in shared memory (the
-//              128-byte-swizzled K-major layout the P @ V MMA reads); combine the row max across the four parts,
-//              then the two exact softmax passes (partial sums of exp_lut combined the same way, then
-//              (e*one + S/2) / S as a multiply by a per-row invariant-divisor magic number), then O from TMEM ->
-//              requant -> global
+//              128-byte-swizzled K-major layout the P @ V MMA reads) once the previous tile's P V MMA has read it;
+//              then the previous tile's O epilogue (TMEM -> requant -> global, off the tile boundary); combine the
+//              row max across the four parts, then the two exact softmax passes (partial sums of exp_lut combined
+//              the same way, then (e*one + S/2) / S as a multiply by a per-row invariant-divisor magic number)
 // The whole score row (up to 1024 keys, int8) stays in shared memory, so the row max and row sum are exact before
 // any probability is formed, as the reference's three-stage loop nest requires; an online (rescaled) softmax
 // would not be bit-exact.
@@ -47,6 +48,8 @@ struct AttnCfg {
   static constexpr int T_BYTES = 128 * HD;              // a K tile (128 keys x hd) or a V^T slab (hd x 128 keys)
   static constexpr int MAX_SLABS = 8;                   // T2 <= 1024
   static constexpr int P_SLAB = 128 * 128;
+  static constexpr int NSB = 3;                         // score buffers in TMEM (128 columns each)
+  static constexpr int O_COL = NSB * 128;               // the O accumulator (hd columns) after them
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + KS * T_BYTES;
@@ -54,7 +57,7 @@ struct AttnCfg {
   static constexpr int OFF_LUT = OFF_P + MAX_SLABS * P_SLAB;
   static constexpr int OFF_RED = OFF_LUT + 1024 * LUT_COPIES;       // [2][4][128] int32: row max, row sum partials
   static constexpr int OFF_BAR = OFF_RED + 4096;
-  static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 4 + 2;
+  static constexpr int NBAR = 2 + 2 * KS + 2 * VS + 2 * NSB + 2 * MAX_SLABS + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
   // Q / K tiles: rows of HD bytes. 64-byte rows use the 64-byte swizzle (8-row atoms of 512 B), 128-byte rows
@@ -134,8 +137,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
   uint64_t *qfull = bars, *qempty = bars + 1;
   uint64_t *kfull = bars + 2, *kempty = kfull + Cfg::KS;
   uint64_t *vfull = kempty + Cfg::KS, *vempty = vfull + Cfg::VS;
-  uint64_t *sfull = vempty + Cfg::VS, *sempty = sfull + 2;
-  uint64_t *pready = sempty + 2, *ofull = pready + 1;
+  uint64_t *sfull = vempty + Cfg::VS, *sempty = sfull + Cfg::NSB;
+  uint64_t *pslab = sempty + Cfg::NSB;     // pslab[j]: P slab j holds probabilities (512 softmax arrivals)
+  uint64_t *pfree = pslab + Cfg::MAX_SLABS;  // pfree[j]: the P V MMA has read P slab j (committed by the MMA)
+  uint64_t *ofull = pfree + Cfg::MAX_SLABS;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Cfg::OFF_MISC);
   volatile int *abort = reinterpret_cast<volatile int *>(smem + Cfg::OFF_MISC + 4);
   int32_t *lut = reinterpret_cast<int32_t *>(smem + Cfg::OFF_LUT);   // entry i of copy c at word i*COPIES + c
@@ -148,8 +153,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     mbar_init(qempty, 1);
     for (int i = 0; i < Cfg::KS; ++i) { mbar_init(&kfull[i], 1); mbar_init(&kempty[i], 1); }
     for (int i = 0; i < Cfg::VS; ++i) { mbar_init(&vfull[i], 1); mbar_init(&vempty[i], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&sfull[i], 1); mbar_init(&sempty[i], ATTN_SOFTMAX_THREADS); }
-    mbar_init(pready, ATTN_SOFTMAX_THREADS);
+    for (int i = 0; i < Cfg::NSB; ++i) { mbar_init(&sfull[i], 1); mbar_init(&sempty[i], ATTN_SOFTMAX_THREADS); }
+    for (int i = 0; i < Cfg::MAX_SLABS; ++i) { mbar_init(&pslab[i], ATTN_SOFTMAX_THREADS); mbar_init(&pfree[i], 1); }
     mbar_init(ofull, 1);
     *abort = 0;
     fence_mbar_init();
@@ -221,10 +226,11 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       constexpr uint32_t idesc_pv = idesc_i8(128, HD);
       const uint32_t sq = smem_u32(smem + Cfg::OFF_Q);
       uint32_t gk = 0, gv = 0, gs = 0;
+      uint32_t pph = 0;                 // bit j: parity of pslab[j]'s next phase (a tile completes slabs 0..nkv-1)
       // S = Q K_j^T for the next K tile into the next S buffer (the tile's Q is resident)
       auto issue_s = [&]() -> bool {
-        const int sb = gs & 1, st = gk % Cfg::KS;
-        if (!mbar_wait(&sempty[sb], ((gs >> 1) & 1) ^ 1, abort, p.flags, p.op_index)) return false;
+        const int sb = gs % Cfg::NSB, st = gk % Cfg::KS;
+        if (!mbar_wait(&sempty[sb], ((gs / Cfg::NSB) & 1) ^ 1, abort, p.flags, p.op_index)) return false;
         if (!mbar_wait(&kfull[st], (gk / Cfg::KS) & 1, abort, p.flags, p.op_index)) return false;
         tc_fence_after();
         const uint32_t sk = smem_u32(smem + Cfg::OFF_K + st * Cfg::T_BYTES);
@@ -240,39 +246,42 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       };
       bool ok = true;
       int t = attn_item(0, ntiles);
-      if (t >= 0) {                     // the first tile's first two score MMAs
+      if (t >= 0) {                     // the first tile's first NSB score MMAs
         const AttnTile w = attn_tile(p, t);
         ok = mbar_wait(qfull, 0, abort, p.flags, p.op_index);
         tc_fence_after();
-        for (int j = 0; ok && j < min(2, w.nkv); ++j) ok = issue_s();
+        for (int j = 0; ok && j < min(Cfg::NSB, w.nkv); ++j) ok = issue_s();
       }
       for (int k = 0; ok && t >= 0; ++k) {
         const AttnTile w = attn_tile(p, t);
-        for (int j = 2; ok && j < w.nkv; ++j) ok = issue_s();
+        for (int j = Cfg::NSB; ok && j < w.nkv; ++j) ok = issue_s();
         if (!ok) break;
         mma_commit(qempty);             // the Q buffer is free once this tile's score MMAs are done
-        // the next tile's first two score MMAs overlap this tile's softmax passes
+        // the next tile's first NSB score MMAs overlap this tile's softmax passes
         const int tn = attn_item(k + 1, ntiles);
         if (tn >= 0) {
           const AttnTile wn = attn_tile(p, tn);
           if (!mbar_wait_idle(qfull, (k + 1) & 1, abort, p.flags, p.op_index)) break;
           tc_fence_after();
-          for (int j = 0; ok && j < min(2, wn.nkv); ++j) ok = issue_s();
+          for (int j = 0; ok && j < min(Cfg::NSB, wn.nkv); ++j) ok = issue_s();
           if (!ok) break;
         }
-        if (!mbar_wait_idle(pready, k & 1, abort, p.flags, p.op_index)) break;
-        tc_fence_after();
+        // O = sum_j P_j V_j, slab by slab as the softmax warps finish each slab's probabilities, so the MMAs and
+        // the V^T loads they free ring slots for run under the rest of the probability pass
         for (int j = 0; ok && j < w.nkv; ++j, ++gv) {
           const int st = gv % Cfg::VS;
+          if (!mbar_wait_idle(&pslab[j], (pph >> j) & 1u, abort, p.flags, p.op_index)) { ok = false; break; }
+          pph ^= 1u << j;
           if (!mbar_wait(&vfull[st], (gv / Cfg::VS) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sp = smem_u32(pbuf + j * Cfg::P_SLAB);
           const uint32_t sv = smem_u32(smem + Cfg::OFF_V + st * Cfg::T_BYTES);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_i8(tmem + 256, kmajor_desc(sp + 32 * kk, 2u, 1024u), kmajor_desc(sv + 32 * kk, 2u, 1024u),
+            mma_i8(tmem + Cfg::O_COL, kmajor_desc(sp + 32 * kk, 2u, 1024u), kmajor_desc(sv + 32 * kk, 2u, 1024u),
                    idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
           mma_commit(&vempty[st]);
+          mma_commit(&pfree[j]);
         }
         if (!ok) break;
         mma_commit(ofull);
@@ -291,27 +300,45 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     const int lcopy = lane % Cfg::LUT_COPIES;
     const long long rnd2 = round_term(p.s2);
     uint32_t gs = 0;
-    for (int k = 0, t; (t = attn_item(k, ntiles)) >= 0; ++k) {
-      // every softmax warp takes the same decision to stop (the named barriers below need all 16): the abort word
-      // is OR-reduced across the 512 threads by the barrier itself
-      int stop;
-      asm volatile(
-          "{\n\t.reg .pred P;\n\t"
-          "setp.ne.s32 P, %1, 0;\n\t"
-          "bar.red.or.pred P, 1, 512, P;\n\t"
-          "selp.s32 %0, 1, 0, P;\n\t}"
-          : "=r"(stop)
-          : "r"(*abort)
-          : "memory");
-      if (stop) break;
+    uint32_t fph = 0;                                // bit j: parity of P slab j's uses so far
+    // O = P V of a finished tile: TMEM -> requant -> merged-heads output row. The last HD/32 parts take 32
+    // columns each: their columns of a causal tile's diagonal slab are the ones with the fewest kept scores, so
+    // these are the warps with the least probability work. It runs after the next tile's score pass, by which
+    // time the tile's P V MMAs are long done, so no warp waits on them at a tile boundary.
+    const int opart = part - (4 - HD / 32);
+    auto o_epilogue = [&](const AttnTile &w, int k) {
+      const int row = w.q0 + r;
+      if (opart >= 0 && __all_sync(0xffffffffu, mbar_wait(ofull, k & 1, abort, p.flags, p.op_index))) {
+        tc_fence_after();
+        int32_t acc[32];
+        tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(Cfg::O_COL + opart * 32), acc);
+        uint32_t wq[8];
+        int v[32];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) v[q] = (int)clampi(((long long)acc[q] * p.m2 + rnd2) >> p.s2, -128, 127);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) wq[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        if (row < p.T1) {
+          int8_t *orow = p.out + (int64_t)w.b * p.o_bs + (int64_t)row * p.o_rs + (int64_t)w.h * HD + opart * 32;
+          uint4 *d4 = reinterpret_cast<uint4 *>(orow);
+          d4[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+          d4[1] = make_uint4(wq[4], wq[5], wq[6], wq[7]);
+        }
+        tc_fence_before();
+      }
+    };
+    AttnTile prev;
+    int k = 0;
+    bool stopped = false;
+    for (int t; (t = attn_item(k, ntiles)) >= 0; ++k) {
       const AttnTile w = attn_tile(p, t);
       const int row = w.q0 + r;
       const int kept = p.causal ? min(row + 1, p.T2) : p.T2;
       int mx = -128;
       bool ok = true;
       for (int j = 0; j < w.nkv; ++j, ++gs) {
-        const int sb = gs & 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(&sfull[sb], (gs >> 1) & 1, abort, p.flags, p.op_index));
+        const int sb = gs % Cfg::NSB;
+        ok = __all_sync(0xffffffffu, mbar_wait(&sfull[sb], (gs / Cfg::NSB) & 1, abort, p.flags, p.op_index));
         if (!ok) break;                     // warp-uniform: the TMEM load below is .sync.aligned
         tc_fence_after();
         int32_t acc[32];
@@ -337,6 +364,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
 #pragma unroll
         for (int q = 0; q < 8; ++q)
           wq[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]) ^ 0x80808080u;
+        // P slab j still feeds the previous tile's P V MMA until pfree[j] completes
+        ok = __all_sync(0xffffffffu, mbar_wait(&pfree[j], ((fph >> j) & 1u) ^ 1u, abort, p.flags, p.op_index));
+        fph ^= 1u << j;
+        if (!ok) break;
         uint8_t *slab = pbuf + j * Cfg::P_SLAB;
         *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part)) = make_uint4(wq[0], wq[1], wq[2], wq[3]);
         *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part + 1)) = make_uint4(wq[4], wq[5], wq[6], wq[7]);
@@ -345,8 +376,21 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       }
       // row max over the 4 parts (clamped: the raw scores were tracked). The max and the sum have their own
       // partial arrays, so a warp that runs ahead into the next tile cannot overwrite what a slower one still reads.
+      if (k > 0 && ok) o_epilogue(prev, k - 1);
+      prev = w;
       red_max[part * 128 + r] = min(127, mx);
-      asm volatile("bar.sync 1, 512;" ::: "memory");
+      // every softmax warp takes the same decision to stop (the named barriers need all 16): the abort word is
+      // OR-reduced across the 512 threads by this barrier itself
+      int stop;
+      asm volatile(
+          "{\n\t.reg .pred P;\n\t"
+          "setp.ne.s32 P, %1, 0;\n\t"
+          "bar.red.or.pred P, 1, 512, P;\n\t"
+          "selp.s32 %0, 1, 0, P;\n\t}"
+          : "=r"(stop)
+          : "r"(*abort)
+          : "memory");
+      if (stop) { stopped = true; break; }
       mx = max(max(red_max[r], red_max[128 + r]), max(red_max[256 + r], red_max[384 + r]));
       // a kept score x <= mx is stored as u = x + 128, and lut[x - mx + 255] = lut[u + 127 - mx]: lutc[u * COPIES]
       // is that entry in this lane's copy (index 0..255 for every kept u)
@@ -424,29 +468,11 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           }
           *reinterpret_cast<uint4 *>(slab + off) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
         }
-      }
-      fence_proxy_async();
-      mbar_arrive(pready);
-      // O = P V from TMEM -> requant -> merged-heads output row (parts 0 .. HD/32-1 take 32 columns each)
-      if (ok && part < HD / 32 && __all_sync(0xffffffffu, mbar_wait(ofull, k & 1, abort, p.flags, p.op_index))) {
-        tc_fence_after();
-        int32_t acc[32];
-        tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(256 + part * 32), acc);
-        uint32_t wq[8];
-        int v[32];
-#pragma unroll
-        for (int q = 0; q < 32; ++q) v[q] = (int)clampi(((long long)acc[q] * p.m2 + rnd2) >> p.s2, -128, 127);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) wq[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        if (row < p.T1) {
-          int8_t *orow = p.out + (int64_t)w.b * p.o_bs + (int64_t)row * p.o_rs + (int64_t)w.h * HD + part * 32;
-          uint4 *d4 = reinterpret_cast<uint4 *>(orow);
-          d4[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
-          d4[1] = make_uint4(wq[4], wq[5], wq[6], wq[7]);
-        }
-        tc_fence_before();
+        fence_proxy_async();                // this thread's part of slab j is final: the P V MMA may read it
+        mbar_arrive(&pslab[j]);
       }
     }
+    if (!stopped && k > 0) o_epilogue(prev, k - 1);
   }
   tc_fence_before();
   __syncthreads();
