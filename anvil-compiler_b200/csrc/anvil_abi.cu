@@ -253,9 +253,23 @@ static int gemm_out_map(Launch &L) {
   GemmParams &p = L.gp;
   memset(&L.mapC, 0, sizeof L.mapC);
   p.tma_store = 0;
-  if (!L.tc || L.bn != 256 || p.out_bytes != 1 || p.o_cstride != 1 || p.o_group != 0 || !aligned16(p.out) ||
-      p.o_rstride % 16 != 0 || (p.batch > 1 && p.o_bstride % 16 != 0) || p.M > (1ll << 31) - 1 ||
+  if (!L.tc || L.bn != 256 || p.out_bytes != 1 || !aligned16(p.out) || p.M > (1ll << 31) - 1 ||
       p.N > (1ll << 31) - 1)
+    return ANVIL_OK;
+  // head-major transposed output (the V^T layout the fused attention reads): element (r, c) at
+  // (r / T) * N * T + c * T + r % T with T = o_group; each warp's 32 rows stay inside one group
+  const int64_t T = p.o_group;
+  if (p.batch == 1 && T > 0 && T % 32 == 0 && p.M % T == 0 && p.o_rstride == 1 && p.o_cstride == T &&
+      p.o_gstride == p.N * T && T <= (1ll << 31) - 1) {
+    const uint64_t cdims[3] = {(uint64_t)T, (uint64_t)p.N, (uint64_t)(p.M / T)};
+    const uint64_t cstr[2] = {(uint64_t)T, (uint64_t)(p.N * T)};
+    const uint32_t cbox[3] = {32, 128, 1};
+    int rc = make_map(&L.mapC, p.out, 3, cdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    p.tma_store = 2;
+    return ANVIL_OK;
+  }
+  if (p.o_cstride != 1 || p.o_group != 0 || p.o_rstride % 16 != 0 || (p.batch > 1 && p.o_bstride % 16 != 0))
     return ANVIL_OK;
   const uint64_t cdims[3] = {(uint64_t)p.N, (uint64_t)p.M, (uint64_t)p.batch};
   const uint64_t cstr[2] = {(uint64_t)p.o_rstride, (uint64_t)p.o_bstride};

@@ -39,7 +39,8 @@ struct GemmParams {
   const void *res;
   int res_bytes, y_bytes, shift2;
   int ma, mb;
-  // tc path: 1 = the output leaves through shared-memory staging and TMA tile stores (i8, row-major, BN = 256)
+  // tc path, BN = 256, i8 output through shared-memory staging and TMA tile stores: 1 = row-major; 2 = the
+  // head-major transposed layout (element (r, c) at (r / o_group) * o_gstride + c * o_group + r % o_group)
   int tma_store;
 };
 
@@ -348,8 +349,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // TMA-store epilogue: this warp's 32 rows x 128 columns of the tile are packed into its staging tile (row r
     // at r*128 bytes, 16-byte chunk c at position c ^ (r & 7), the 128-byte swizzle of the output tensor map)
     // and leave as one tile store; edges are clipped by the tensor map
-    const bool tma_st = p.tma_store != 0;
-    uint8_t *stg = smem + Cfg::STG_OFF + (warp - 2) * 4096 + lane * 128;
+    // The transposed mode stages the warp's 32 rows x 128 columns as 128 column-rows of 32 bytes (lane = byte).
+    const int tmode = p.tma_store;
+    const bool tma_st = tmode != 0;
+    uint8_t *stg_w = smem + Cfg::STG_OFF + (warp - 2) * 4096;
+    uint8_t *stg = stg_w + lane * 128;
+    // the folded bias of a chunk's 32 columns, loaded one chunk ahead like the residual
+    const bool bias_pre = p.bias && !p.check;
     const uint32_t c2 = (uint32_t)(s2 ? 1 << (s2 - 1) : 0) - 128u * ((uint32_t)p.ma + (uint32_t)p.mb);
     bool bad = false;
     for (int64_t t = blockIdx.x; t < p.tiles; t += gridDim.x) {
@@ -371,6 +377,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
       };
       if (RES) prefetch(0, rcur, rcur_ok);
+      auto bias_at = [&](int ci) -> int {
+        const int64_t c = nb * BN + half * (BN / 2) + ci * 32 + lane;
+        return c < p.N ? __ldg(p.bias + c) : 0;
+      };
+      int bcur = bias_pre ? bias_at(0) : 0, bnxt = 0;
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aphase, abort, p.flags, p.op_index))) break;
       tc_fence_after();
       if (tma_st) {                                    // the previous tile's store has read the staging tile
@@ -384,6 +395,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int ci = 0; ci < NCH; ++ci) {
         const int c0 = half * (BN / 2) + ci * 32;
         if (RES && ci + 1 < NCH) prefetch(ci + 1, rnxt, rnxt_ok);
+        if (bias_pre && ci + 1 < NCH) bnxt = bias_at(ci + 1);
         int32_t r[32];
         tmem_ld32(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c0), r);
         const int64_t col0 = nb * BN + c0;
@@ -399,7 +411,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           int br[32];
           if (p.bias) {
             __syncwarp();
-            bslot[lane] = col0 + lane < p.N ? p.bias[col0 + lane] : 0;
+            bslot[lane] = bcur;
             __syncwarp();
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
@@ -450,12 +462,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int q = 0; q < 32; ++q) v[q] = residual_add<OB>(min(yhi, max(ylo, y[q])), row_ok ? rv[q] : 0, p);
           }
         }
-        if (tma_st) {
+        if (tmode == 1) {
           uint32_t w[8];
 #pragma unroll
           for (int q = 0; q < 8; ++q) w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
           st_shared_v4(stg + (((2 * ci) ^ (lane & 7)) << 4), w[0], w[1], w[2], w[3]);
           st_shared_v4(stg + (((2 * ci + 1) ^ (lane & 7)) << 4), w[4], w[5], w[6], w[7]);
+        } else if (tmode == 2) {            // column q of the chunk -> staging row ci*32 + q, this lane's byte
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint32_t w = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+#pragma unroll
+            for (int k2 = 0; k2 < 4; ++k2) st_shared_u8(stg_w + (ci * 32 + 4 * q + k2) * 32 + lane, w >> (8 * k2));
+          }
         } else if (row_ok) {
           const int cnt = (int)(p.N - col0 < 32 ? p.N - col0 : 32);
           if (p.o_cstride == 1) {
@@ -472,6 +491,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           rcur[1] = rnxt[1];
           rcur_ok = rnxt_ok;
         }
+        bcur = bnxt;
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -480,10 +500,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) {
-          const uint8_t *src = smem + Cfg::STG_OFF + (warp - 2) * 4096;
-          const int x = (int)(nb * BN + half * (BN / 2)), y = (int)(mb * TC_BM + lane_base);
-          if (p.batch > 1) tma_store_3d(&tmC, src, x, y, (int)bb);
-          else tma_store_2d(&tmC, src, x, y);
+          const int64_t r0 = mb * TC_BM + lane_base;
+          const int c0 = (int)(nb * BN + half * (BN / 2));
+          if (tmode == 2) tma_store_3d(&tmC, stg_w, (int)(r0 % p.o_group), c0, (int)(r0 / p.o_group));
+          else if (p.batch > 1) tma_store_3d(&tmC, stg_w, c0, (int)r0, (int)bb);
+          else tma_store_2d(&tmC, stg_w, c0, (int)r0);
           bulk_commit();
         }
       }

@@ -166,7 +166,7 @@ def test_embed_index_error():
 @pytest.mark.parametrize("T,C,nh,causal,T2", [(256, 128, 2, True, None), (128, 128, 2, False, None),
                                               (208, 256, 2, True, None), (1024, 768, 12, True, None),
                                               (96, 128, 2, False, 160), (64, 512, 4, True, None),
-                                              (200, 128, 2, True, None)])
+                                              (200, 128, 2, True, None), (96, 384, 3, True, None)])
 def test_fused_attention_bit_exact(T, C, nh, causal, T2):
     from graphs import attention_graph
     m, c, x = attention_graph(T + C + nh, T, C, nh, causal, T2)
