@@ -247,7 +247,7 @@ static int resolve(anvil_model *m, const anvil_op &op, int slot, uint64_t bytes,
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// tc GEMMs with i8 row-major outputs of 256-column tiles store through TMA (32 rows x 128 bytes per epilogue warp);
+// tc GEMMs with i8 row-major outputs of 256-column tiles store through TMA (32 rows x 64 bytes per epilogue warp);
 // the tensor map goes in L.mapC and sets gp.tma_store. Other outputs keep the per-lane global stores.
 static int gemm_out_map(Launch &L) {
   GemmParams &p = L.gp;
@@ -263,7 +263,7 @@ static int gemm_out_map(Launch &L) {
       p.o_gstride == p.N * T && T <= (1ll << 31) - 1) {
     const uint64_t cdims[3] = {(uint64_t)T, (uint64_t)p.N, (uint64_t)(p.M / T)};
     const uint64_t cstr[2] = {(uint64_t)T, (uint64_t)(p.N * T)};
-    const uint32_t cbox[3] = {32, 128, 1};
+    const uint32_t cbox[3] = {32, 64, 1};               // one epilogue warp's 32 rows x 64 columns, transposed
     int rc = make_map(&L.mapC, p.out, 3, cdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     p.tma_store = 2;
@@ -273,8 +273,8 @@ static int gemm_out_map(Launch &L) {
     return ANVIL_OK;
   const uint64_t cdims[3] = {(uint64_t)p.N, (uint64_t)p.M, (uint64_t)p.batch};
   const uint64_t cstr[2] = {(uint64_t)p.o_rstride, (uint64_t)p.o_bstride};
-  const uint32_t cbox[3] = {128, 32, 1};
-  int rc = make_map(&L.mapC, p.out, p.batch > 1 ? 3 : 2, cdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  const uint32_t cbox[3] = {64, 32, 1};                  // one epilogue warp's 32 rows x 64 columns
+  int rc = make_map(&L.mapC, p.out, p.batch > 1 ? 3 : 2, cdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
   p.tma_store = 1;
   return ANVIL_OK;

@@ -145,8 +145,8 @@ __global__ void __launch_bounds__(256) qgemm_simt_kernel(GemmParams p) {
 
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 128;                // bytes of K per stage = one 128-byte swizzle row
-constexpr int TC_EPI_WARPS = 8;           // two warps per TMEM lane quarter, each owning half the tile's columns
-constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;   // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int TC_EPI_WARPS = 16;          // four warps per TMEM lane quarter, each owning a quarter of the columns
+constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;   // warp 0 TMA, warp 1 MMA, warps 2-17 epilogue
 constexpr int TC_SMEM_RING = 192 * 1024;  // bytes of A/B stages
 
 template <int BN>
@@ -159,15 +159,19 @@ struct TcCfg {
   // A LUT epilogue keeps the LUT replicated once per lane as int32 words (32 KB: entry e of lane l at word
   // 32 e + l, conflict-free lookups) in the last LUT_STAGES ring stages, and runs with the rest of the ring.
   static constexpr int LUT_STAGES = (32 * 1024 + STAGE_BYTES - 1) / STAGE_BYTES;
-  // After the ring: the output staging (one 32-row x 128-byte, 128-byte-swizzled tile per epilogue warp), the
-  // barriers full[S], empty[S], tmem_full[2], tmem_empty[2], the TMEM base slot and abort word, and a 128-byte
-  // bias staging slot per epilogue warp.
+  // Each epilogue warp owns 32 accumulator rows (its TMEM lane quarter) x COLS columns, drained 16 at a time.
+  static constexpr int COLS = BN / 4;
+  static constexpr int NSC = COLS / 16;
+  // After the ring: the output staging (one 32-row x COLS-byte tile per epilogue warp), the barriers full[S],
+  // empty[S], tmem_full[2], tmem_empty[2], the TMEM base slot and abort word, and a 64-byte bias staging slot per
+  // epilogue warp.
   static constexpr int STG_OFF = STAGES * STAGE_BYTES;
-  static constexpr int STG_BYTES = TC_EPI_WARPS * 4096;
+  static constexpr int STG_WARP = 32 * COLS;
+  static constexpr int STG_BYTES = TC_EPI_WARPS * STG_WARP;
   static constexpr int BAR_OFF = STG_OFF + STG_BYTES;
   static constexpr int MISC_OFF = BAR_OFF + (2 * STAGES + 4) * 8;
   static constexpr int BST_OFF = MISC_OFF + 16;
-  static constexpr int SMEM_BYTES = BST_OFF + TC_EPI_WARPS * 128 + 1024;   // + 1 KB slack to align the ring
+  static constexpr int SMEM_BYTES = BST_OFF + TC_EPI_WARPS * 64 + 1024;   // + 1 KB slack to align the ring
 };
 
 // Load 32 consecutive int8 / int16 values of a row (vector loads when the chunk is whole and aligned).
@@ -198,6 +202,58 @@ __device__ __forceinline__ void load_row32(const void *base, int bytes, int64_t 
 #pragma unroll
       for (int q = 0; q < 32; ++q) rv[q] = q < count ? (int)src[q] : 0;
     }
+  }
+}
+
+// Load 16 consecutive int8 / int16 values of a row (vector loads when the chunk is whole and aligned).
+__device__ __forceinline__ void load_row16(const void *base, int bytes, int64_t elem, int count, int (&rv)[16]) {
+  if (bytes == 1) {
+    const int8_t *src = reinterpret_cast<const int8_t *>(base) + elem;
+    if (count == 16 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+      const uint4 a = reinterpret_cast<const uint4 *>(src)[0];
+      const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+      for (int q = 0; q < 16; ++q) rv[q] = (int)(int8_t)(w[q >> 2] >> (8 * (q & 3)));
+    } else {
+#pragma unroll
+      for (int q = 0; q < 16; ++q) rv[q] = q < count ? (int)src[q] : 0;
+    }
+  } else {
+    const int16_t *src = reinterpret_cast<const int16_t *>(base) + elem;
+    if (count == 16 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+      const uint4 a = reinterpret_cast<const uint4 *>(src)[0], b = reinterpret_cast<const uint4 *>(src)[1];
+      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int q = 0; q < 16; ++q) rv[q] = (int)(int16_t)(w[q >> 1] >> (16 * (q & 1)));
+    } else {
+#pragma unroll
+      for (int q = 0; q < 16; ++q) rv[q] = q < count ? (int)src[q] : 0;
+    }
+  }
+}
+
+// Store 16 consecutive results of one output row: 16-byte vector stores when the whole chunk is in range and
+// aligned, element stores otherwise.
+template <int OB>
+__device__ __forceinline__ void store_row16(typename IntOf<OB>::T *dst, const int (&v)[16], int count) {
+  if (count == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    if (OB == 1) {                      // saturating pack: values may arrive unclamped
+      uint32_t w[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      uint32_t w[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) w[q] = (uint32_t)(uint16_t)v[2 * q] | ((uint32_t)(uint16_t)v[2 * q + 1] << 16);
+      uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+      d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 16; ++q)
+      if (q < count) dst[q] = (typename IntOf<OB>::T)(OB == 1 ? min(127, max(-128, v[q])) : v[q]);
   }
 }
 
@@ -330,12 +386,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..9)
-    // warp w reads TMEM lane quarter (w % 4) and columns [half*BN/2, half*BN/2 + BN/2), half = (w - 2) / 4
-    constexpr int NCH = BN / 64;                         // 32-column chunks per warp and tile
+    // ------------------------------------------------------------------ epilogue (warps 2..17)
+    // warp w reads TMEM lane quarter (w % 4) and columns [cq*COLS, cq*COLS + COLS), cq = (w - 2) / 4, 16 at a time
+    constexpr int NSC = Cfg::NSC;
     const int lane_base = 32 * (warp & 3);
-    const int half = (warp - 2) >> 2;
-    int32_t *bslot = bst + (warp - 2) * 32;
+    const int cq = (warp - 2) >> 2;
+    int32_t *bslot = bst + (warp - 2) * 16;
     int acc = 0;
     uint32_t aphase = 0;
     constexpr int lo = OB == 1 ? -128 : -32768, hi = OB == 1 ? 127 : 32767;
@@ -346,41 +402,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // static int32 proof bounds the true value
     const bool res_fast = RES && p.res_bytes == 1 && p.y_bytes == 1;
     const int s2 = p.shift2;
-    // TMA-store epilogue: this warp's 32 rows x 128 columns of the tile are packed into its staging tile (row r
-    // at r*128 bytes, 16-byte chunk c at position c ^ (r & 7), the 128-byte swizzle of the output tensor map)
-    // and leave as one tile store; edges are clipped by the tensor map
-    // The transposed mode stages the warp's 32 rows x 128 columns as 128 column-rows of 32 bytes (lane = byte).
+    const uint32_t c2 = (uint32_t)(s2 ? 1 << (s2 - 1) : 0) - 128u * ((uint32_t)p.ma + (uint32_t)p.mb);
+    // TMA-store epilogue (BN = 256): this warp's 32 rows x 64 columns are packed into its 2 KB staging tile and
+    // leave as one tile store, edges clipped by the tensor map. Row-major mode: row r at r*64 bytes, 16-byte chunk
+    // c at position c ^ ((r >> 1) & 3) (the 64-byte swizzle of the output map). Transposed mode: 64 column-rows of
+    // 32 bytes, lane = byte.
     const int tmode = p.tma_store;
     const bool tma_st = tmode != 0;
-    uint8_t *stg_w = smem + Cfg::STG_OFF + (warp - 2) * 4096;
-    uint8_t *stg = stg_w + lane * 128;
-    // the folded bias of a chunk's 32 columns, loaded one chunk ahead like the residual
+    uint8_t *stg_w = smem + Cfg::STG_OFF + (warp - 2) * Cfg::STG_WARP;
+    uint8_t *stg = stg_w + lane * Cfg::COLS;
+    // the folded bias of a sub-chunk's 16 columns (lanes 0-15), loaded one sub-chunk ahead like the residual
     const bool bias_pre = p.bias && !p.check;
-    const uint32_t c2 = (uint32_t)(s2 ? 1 << (s2 - 1) : 0) - 128u * ((uint32_t)p.ma + (uint32_t)p.mb);
     bool bad = false;
     for (int64_t t = blockIdx.x; t < p.tiles; t += gridDim.x) {
       const int64_t nb = t % p.n_tiles, rest = t / p.n_tiles;
       const int64_t mb = rest % p.m_tiles, bb = rest / p.m_tiles;
       const int64_t row = mb * TC_BM + lane_base + lane;
       const bool row_ok = row < p.M;
-      // residual words of chunk c of this lane's row, issued one chunk ahead (the first before the accumulator
-      // wait) so the loads overlap the MMAs and the previous chunk's arithmetic
-      uint4 rcur[2], rnxt[2];
+      const int64_t cbase = nb * BN + cq * Cfg::COLS;
+      uint4 rcur = make_uint4(0, 0, 0, 0), rnxt = make_uint4(0, 0, 0, 0);
       bool rcur_ok = false, rnxt_ok = false;
-      auto prefetch = [&](int ci, uint4(&dst)[2], bool &ok) {
-        const int64_t col0 = nb * BN + half * (BN / 2) + ci * 32;
+      auto prefetch = [&](int sc, uint4 &dst, bool &ok) {
+        const int64_t col0 = cbase + sc * 16;
         const int8_t *src = reinterpret_cast<const int8_t *>(p.res) + row * p.N + col0;
-        ok = res_fast && row_ok && col0 + 32 <= p.N && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
-        if (ok) {
-          dst[0] = reinterpret_cast<const uint4 *>(src)[0];
-          dst[1] = reinterpret_cast<const uint4 *>(src)[1];
-        }
+        ok = res_fast && row_ok && col0 + 16 <= p.N && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+        if (ok) dst = *reinterpret_cast<const uint4 *>(src);
       };
-      if (RES) prefetch(0, rcur, rcur_ok);
-      auto bias_at = [&](int ci) -> int {
-        const int64_t c = nb * BN + half * (BN / 2) + ci * 32 + lane;
+      auto bias_at = [&](int sc) -> int {
+        const int64_t c = cbase + sc * 16 + (lane & 15);
         return c < p.N ? __ldg(p.bias + c) : 0;
       };
+      if (RES) prefetch(0, rcur, rcur_ok);
       int bcur = bias_pre ? bias_at(0) : 0, bnxt = 0;
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aphase, abort, p.flags, p.op_index))) break;
       tc_fence_after();
@@ -392,59 +444,57 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int64_t R = p.o_group ? p.o_group : p.M;
       TO *orow = reinterpret_cast<TO *>(p.out) + bb * p.o_bstride + (row / R) * p.o_gstride + (row % R) * p.o_rstride;
 #pragma unroll 1
-      for (int ci = 0; ci < NCH; ++ci) {
-        const int c0 = half * (BN / 2) + ci * 32;
-        if (RES && ci + 1 < NCH) prefetch(ci + 1, rnxt, rnxt_ok);
-        if (bias_pre && ci + 1 < NCH) bnxt = bias_at(ci + 1);
-        int32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c0), r);
+      for (int sc = 0; sc < NSC; ++sc) {
+        const int c0 = cq * Cfg::COLS + sc * 16;
+        if (RES && sc + 1 < NSC) prefetch(sc + 1, rnxt, rnxt_ok);
+        if (bias_pre && sc + 1 < NSC) bnxt = bias_at(sc + 1);
+        int32_t r[16];
+        tmem_ld16(tmem_base + ((uint32_t)lane_base << 16) + (uint32_t)(acc * BN + c0), r);
         const int64_t col0 = nb * BN + c0;
         if (col0 >= p.N) continue;                     // warp-uniform
-        int v[32];
+        int v[16];
         if (p.check) {
 #pragma unroll
-          for (int q = 0; q < 32; ++q)
+          for (int q = 0; q < 16; ++q)
             v[q] = gemm_epi<true>(r[q], (p.bias && col0 + q < p.N) ? p.bias[col0 + q] : 0, p, p.lut, lo, hi, bad);
         } else {
           // the static int32 proof holds: (acc [+ bias]) * M + 2^(s-1) fits int32, so 32-bit wrap-free math is
           // exact; a bias arrives pre-folded as bias*M + 2^(s-1) (ANVIL_F_BIAS_RND)
-          int br[32];
+          int br[16];
           if (p.bias) {
             __syncwarp();
-            bslot[lane] = bcur;
+            if (lane < 16) bslot[lane] = bcur;
             __syncwarp();
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
+            for (int q = 0; q < 4; ++q) {
               const int4 b4 = reinterpret_cast<const int4 *>(bslot)[q];
               br[4 * q] = b4.x; br[4 * q + 1] = b4.y; br[4 * q + 2] = b4.z; br[4 * q + 3] = b4.w;
             }
           } else {
 #pragma unroll
-            for (int q = 0; q < 32; ++q) br[q] = rnd;
+            for (int q = 0; q < 16; ++q) br[q] = rnd;
           }
-          int y[32];
+          int y[16];
 #pragma unroll
-          for (int q = 0; q < 32; ++q) y[q] = (r[q] * m32 + br[q]) >> sh;
+          for (int q = 0; q < 16; ++q) y[q] = (r[q] * m32 + br[q]) >> sh;
           if (!RES) {
             if (OB == 1 && lt) {
               // saturate four at a time, bias the bytes by 128 and look each up in this lane's LUT copy
 #pragma unroll
-              for (int q = 0; q < 8; ++q) {
+              for (int q = 0; q < 4; ++q) {
                 const uint32_t w = pack4_sat_s8(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]) ^ 0x80808080u;
 #pragma unroll
                 for (int k = 0; k < 4; ++k) v[4 * q + k] = lt[ubyte(w, k) * 32];
               }
             } else {
 #pragma unroll
-              for (int q = 0; q < 32; ++q) v[q] = OB == 1 ? y[q] : min(hi, max(lo, y[q]));   // i8 saturates in the pack
+              for (int q = 0; q < 16; ++q) v[q] = OB == 1 ? y[q] : min(hi, max(lo, y[q]));   // i8 saturates in the pack
             }
           } else if (rcur_ok) {
-            const uint4 *rw = rcur;
-            const uint32_t rwv[8] = {rw[0].x ^ 0x80808080u, rw[0].y ^ 0x80808080u, rw[0].z ^ 0x80808080u,
-                                     rw[0].w ^ 0x80808080u, rw[1].x ^ 0x80808080u, rw[1].y ^ 0x80808080u,
-                                     rw[1].z ^ 0x80808080u, rw[1].w ^ 0x80808080u};
+            const uint32_t rwv[4] = {rcur.x ^ 0x80808080u, rcur.y ^ 0x80808080u, rcur.z ^ 0x80808080u,
+                                     rcur.w ^ 0x80808080u};
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
+            for (int q = 0; q < 4; ++q) {
               const uint32_t yw = pack4_sat_s8(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]) ^ 0x80808080u;
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
@@ -455,42 +505,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
           } else {          // fused residual add: y clamped to its own dtype, then res*Ma + y*Mb requantised
             const int ylo = p.y_bytes == 1 ? -128 : -32768, yhi = p.y_bytes == 1 ? 127 : 32767;
-            int rv[32];
-            const int cnt = (int)(p.N - col0 < 32 ? p.N - col0 : 32);
-            if (row_ok) load_row32(p.res, p.res_bytes, row * p.N + col0, cnt, rv);
+            int rv[16];
+            const int cnt = (int)(p.N - col0 < 16 ? p.N - col0 : 16);
+            if (row_ok) load_row16(p.res, p.res_bytes, row * p.N + col0, cnt, rv);
 #pragma unroll
-            for (int q = 0; q < 32; ++q) v[q] = residual_add<OB>(min(yhi, max(ylo, y[q])), row_ok ? rv[q] : 0, p);
+            for (int q = 0; q < 16; ++q) v[q] = residual_add<OB>(min(yhi, max(ylo, y[q])), row_ok ? rv[q] : 0, p);
           }
         }
         if (tmode == 1) {
-          uint32_t w[8];
+          uint32_t w[4];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          st_shared_v4(stg + (((2 * ci) ^ (lane & 7)) << 4), w[0], w[1], w[2], w[3]);
-          st_shared_v4(stg + (((2 * ci + 1) ^ (lane & 7)) << 4), w[4], w[5], w[6], w[7]);
-        } else if (tmode == 2) {            // column q of the chunk -> staging row ci*32 + q, this lane's byte
+          for (int q = 0; q < 4; ++q) w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          st_shared_v4(stg + ((sc ^ ((lane >> 1) & 3)) << 4), w[0], w[1], w[2], w[3]);
+        } else if (tmode == 2) {            // column q of the sub-chunk -> staging row sc*16 + q, this lane's byte
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
+          for (int q = 0; q < 4; ++q) {
             const uint32_t w = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
 #pragma unroll
-            for (int k2 = 0; k2 < 4; ++k2) st_shared_u8(stg_w + (ci * 32 + 4 * q + k2) * 32 + lane, w >> (8 * k2));
+            for (int k2 = 0; k2 < 4; ++k2) st_shared_u8(stg_w + (sc * 16 + 4 * q + k2) * 32 + lane, w >> (8 * k2));
           }
         } else if (row_ok) {
-          const int cnt = (int)(p.N - col0 < 32 ? p.N - col0 : 32);
+          const int cnt = (int)(p.N - col0 < 16 ? p.N - col0 : 16);
           if (p.o_cstride == 1) {
-            store_row32<OB>(orow + col0, v, cnt);
+            store_row16<OB>(orow + col0, v, cnt);
           } else {            // strided columns (head-major transposed output): lanes = consecutive rows
             TO *dst = orow + col0 * p.o_cstride;
 #pragma unroll
-            for (int q = 0; q < 32; ++q)
+            for (int q = 0; q < 16; ++q)
               if (q < cnt) dst[q * p.o_cstride] = (TO)min(hi, max(lo, v[q]));
           }
         }
-        if (RES) {
-          rcur[0] = rnxt[0];
-          rcur[1] = rnxt[1];
-          rcur_ok = rnxt_ok;
-        }
+        rcur = rnxt;
+        rcur_ok = rnxt_ok;
         bcur = bnxt;
       }
       tc_fence_before();
@@ -501,7 +547,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __syncwarp();
         if (lane == 0) {
           const int64_t r0 = mb * TC_BM + lane_base;
-          const int c0 = (int)(nb * BN + half * (BN / 2));
+          const int c0 = (int)cbase;
           if (tmode == 2) tma_store_3d(&tmC, stg_w, (int)(r0 % p.o_group), c0, (int)(r0 / p.o_group));
           else if (p.batch > 1) tma_store_3d(&tmC, stg_w, c0, (int)r0, (int)bb);
           else tma_store_2d(&tmC, stg_w, c0, (int)r0);
