@@ -28,6 +28,8 @@ import numpy as np
 from .ir import graph as g
 
 BACKENDS = ("cuda",)
+PIPELINE_MODELS = 3          # device models (arenas + streams) a pipelined run rotates over
+PIPELINE_TOKENS = 16384      # "auto" pipeline chunk size, in tokens
 
 
 @dataclass(frozen=True)
@@ -39,11 +41,16 @@ class CudaParams:
               the static overflow proof does not hold for the graph
     fuse      apply launch fusions (LUT epilogues, fused attention); keep="all" runs disable them
     gemm      "auto" | "tc" (tcgen05 wherever the shape allows) | "simt" (CUDA-core kernel everywhere)
+    pipeline  chunks a device's share of a run is split into, so one chunk's host<->device copies overlap another
+              chunk's kernels (chunks go round-robin over PIPELINE_MODELS device models, each with its own arena
+              and stream); "auto" picks chunks of about PIPELINE_TOKENS tokens when that gives at least two equal
+              ones, 1 disables it. keep="all" and timing runs are never split.
     """
     devices: tuple = (0,)
     checked: bool | None = None
     fuse: bool = True
     gemm: str = "auto"
+    pipeline: int | str = "auto"
 
     def __post_init__(self):
         if not self.devices or any(not isinstance(d, int) or d < 0 for d in self.devices):
@@ -52,6 +59,8 @@ class CudaParams:
             raise ValueError(f"CudaParams.devices = {self.devices!r}: a device may appear once")
         if self.gemm not in ("auto", "tc", "simt"):
             raise ValueError(f"CudaParams.gemm = {self.gemm!r}: auto, tc or simt")
+        if self.pipeline != "auto" and (not isinstance(self.pipeline, int) or self.pipeline < 1):
+            raise ValueError(f"CudaParams.pipeline = {self.pipeline!r}: 'auto' or a chunk count >= 1")
 
 
 class RunOutput:
@@ -165,6 +174,7 @@ class CompiledModel:
         self._programs = {}          # (batch, keep) -> DeviceProgram
         self._devices = {}           # device -> DeviceModel
         self._pool_size_at_upload = {}
+        self._pipes = {}             # device -> [DeviceModel] for pipelined runs
         self._lock = threading.Lock()
 
     # ------------------------------------------------------------------------------------- programs
@@ -183,6 +193,40 @@ class CompiledModel:
     @property
     def footprint(self) -> int:
         return self.plan.footprint
+
+    def _pipe_models(self, device: int) -> list:
+        """PIPELINE_MODELS replicas on `device` for chunked runs (constants uploaded once each)."""
+        from .runtime.cuda import DeviceModel
+        ms = self._pipes.get(device)
+        if ms is None or self._pool_size_at_upload.get(("pipe", device)) != self._pool.size:
+            for m in ms or []:
+                m.close()
+            blob = self._pool.blob()
+            ms = [DeviceModel(device, blob) for _ in range(PIPELINE_MODELS)]
+            self._pipes[device] = ms
+            self._pool_size_at_upload[("pipe", device)] = self._pool.size
+        return ms
+
+    def _chunks(self, b: int, keep: str, timing: bool) -> int:
+        """How many equal chunks a shard of b samples runs in (1: one launch chain)."""
+        if keep != "outputs" or timing or b < 2:
+            return 1
+        if self.params.pipeline != "auto":
+            n = min(int(self.params.pipeline), b)
+            while b % n:
+                n -= 1
+            return n
+        tokens = b * max(1, self._tokens_per_sample())
+        want = max(1, round(tokens / PIPELINE_TOKENS))
+        for n in sorted(range(2, b + 1), key=lambda k: (abs(k - want), k)):
+            if b % n == 0 and n <= want * 2:
+                return n
+        return 1
+
+    def _tokens_per_sample(self) -> int:
+        """Rows of the first input per sample (sequence length for (T, d) or (T,) inputs)."""
+        shape = self.meta[self.inputs[0]][1]
+        return int(shape[0]) if len(shape) else 1
 
     def _device_model(self, device: int):
         from .runtime.cuda import DeviceModel
@@ -361,6 +405,9 @@ class CompiledModel:
         return ints, results[0][1], [(d, hi - lo) for d, lo, hi in shards]
 
     def _run_shard(self, device, bound, b, keep, timing, out=None):
+        n = self._chunks(b, keep, timing)
+        if n > 1 and self._pipelinable(self.program(b // n, keep)):
+            return self._run_pipelined(device, bound, b, n, out)
         prog = self.program(b, keep)
         dm = self._device_model(device)
         if dm.prepared_key != (b, keep):
@@ -393,6 +440,62 @@ class CompiledModel:
         for sym in self.inputs:
             ints.setdefault(sym, bound[sym])
         return ints, kus
+
+    def _pipelinable(self, prog) -> bool:
+        """Every graph output is a whole, contiguous arena buffer (copied per chunk straight into its rows)."""
+        for sym, v in self._readable(prog, "outputs").items():
+            nbytes = int(np.prod(self.meta[sym][1], dtype=np.int64)) * prog.batch * {"i8": 1, "i16": 2, "i32": 4}[
+                self.meta[sym][2]]
+            if not v.contiguous or prog.buffers[v.root] != nbytes:
+                return False
+        return True
+
+    def _run_pipelined(self, device, bound, b, n, out=None):
+        """The shard as n equal chunks enqueued round-robin on PIPELINE_MODELS device models: while one chunk's
+        kernels run, the next chunk's inputs are copied in and the previous chunk's outputs copied out (each model
+        has its own stream and arena; the copies go straight between the caller's arrays and the device)."""
+        from .runtime.program import NP
+        cb = b // n
+        prog = self.program(cb, "outputs")
+        models = self._pipe_models(device)
+        for dm in models:
+            if dm.prepared_key != (cb, "outputs"):
+                dm.prepare(prog.ops, prog.plan.arena, key=(cb, "outputs"))
+        ins = {sym: np.ascontiguousarray(bound[sym], dtype=NP[dtype]) for sym, (_, _, dtype) in prog.inputs.items()}
+        want = self._readable(prog, "outputs")
+        res = {}
+        for sym, v in want.items():
+            if out and sym in out and v.contiguous and out[sym].nbytes == n * prog.buffers[v.root]:
+                res[sym] = out[sym]
+            else:
+                res[sym] = np.empty((b,) + tuple(self.meta[sym][1]), dtype=NP[self.meta[sym][2]])
+        used = models[:min(n, len(models))]
+        for dm in used:
+            dm.clear_flags()
+        try:
+            for i in range(n):
+                lo, hi = i * cb, (i + 1) * cb
+                dm = used[i % len(used)]
+                dm.enqueue([(off, ins[sym][lo:hi]) for sym, (off, _, _) in prog.inputs.items()],
+                           [(prog.plan.addresses[v.root], res[sym][lo:hi]) for sym, v in want.items()])
+        finally:
+            errs = []
+            for dm in used:
+                try:
+                    dm.wait()
+                except Exception as e:             # every stream drained before the first error is raised
+                    errs.append(e)
+            if errs:
+                raise errs[0]
+        ints = {}
+        for sym in want:
+            ints[sym] = res[sym]
+            if out and sym in out and res[sym] is not out[sym]:
+                out[sym][...] = res[sym]
+                ints[sym] = out[sym]
+        for sym in self.inputs:
+            ints.setdefault(sym, bound[sym])
+        return ints, None
 
     def _readable(self, prog, keep):
         want = {}

@@ -28,7 +28,8 @@ KIND_NAMES = {OP_GEMM: "gemm", OP_LUT: "lut", OP_LUT_MUL: "lut_mul", OP_ADD_REQU
               OP_ATTENTION: "attention", OP_COPY: "copy"}
 
 EXPORTS = ("anvil_abi_version", "anvil_last_error", "anvil_device_count", "anvil_cuda_init", "anvil_model_create",
-           "anvil_model_prepare", "anvil_model_run", "anvil_model_run_device", "anvil_model_read",
+           "anvil_model_prepare", "anvil_model_run", "anvil_model_enqueue", "anvil_model_clear_flags",
+           "anvil_model_wait", "anvil_model_run_device", "anvil_model_read",
            "anvil_model_write", "anvil_model_arena", "anvil_model_free", "anvil_gemm_requant")
 
 
@@ -70,6 +71,9 @@ def load_library(path: str | os.PathLike | None = None):
             "anvil_model_run": ([vp, ctypes.POINTER(AnvilIO), i32, ctypes.POINTER(AnvilIO), i32,
                                  ctypes.POINTER(ctypes.c_float)], i32),
             "anvil_model_run_device": ([vp, i32, i32, ctypes.POINTER(ctypes.c_float)], i32),
+            "anvil_model_enqueue": ([vp, ctypes.POINTER(AnvilIO), i32, ctypes.POINTER(AnvilIO), i32], i32),
+            "anvil_model_clear_flags": ([vp], i32),
+            "anvil_model_wait": ([vp], i32),
             "anvil_model_read": ([vp, u64, vp, u64], i32),
             "anvil_model_write": ([vp, u64, vp, u64], i32),
             "anvil_model_arena": ([vp, ctypes.POINTER(u64), ctypes.POINTER(u64)], i32),
@@ -129,6 +133,20 @@ class DeviceModel:
         us = (ctypes.c_float * max(1, self.n_ops))() if timing else None
         check(self.lib.anvil_model_run(self._h, ins, len(inputs), outs, len(outputs), us), "anvil_model_run")
         return list(us)[: self.n_ops] if timing else None
+
+    def enqueue(self, inputs: list[tuple[int, np.ndarray]], outputs: list[tuple[int, np.ndarray]]):
+        """anvil_model_enqueue: copies in, the launch chain, copies out, on this model's stream, without waiting.
+        The host arrays must stay alive (and unmodified) until wait() returns."""
+        ins = (AnvilIO * max(1, len(inputs)))(*[AnvilIO(o, a.ctypes.data, a.nbytes) for o, a in inputs])
+        outs = (AnvilIO * max(1, len(outputs)))(*[AnvilIO(o, a.ctypes.data, a.nbytes) for o, a in outputs])
+        check(self.lib.anvil_model_enqueue(self._h, ins, len(inputs), outs, len(outputs)), "anvil_model_enqueue")
+
+    def clear_flags(self):
+        check(self.lib.anvil_model_clear_flags(self._h), "anvil_model_clear_flags")
+
+    def wait(self):
+        """Synchronise this model's stream and raise if a device check fired since clear_flags()."""
+        check(self.lib.anvil_model_wait(self._h), "anvil_model_wait")
 
     def run_device(self, iters: int = 1, use_graph: bool = True) -> float:
         ms = ctypes.c_float(0)

@@ -727,22 +727,73 @@ extern "C" int anvil_model_run(anvil_model *m, const anvil_io *inputs, int n_inp
   return check_flags(m, hflags);
 }
 
+// Capture the launch list once as a CUDA graph (re-captured after every anvil_model_prepare).
+static int ensure_graph(anvil_model *m) {
+  if (m->graph) return ANVIL_OK;
+  cudaGraph_t g;
+  CK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = ANVIL_OK;
+  for (auto &L : m->launches)
+    if ((rc = launch_op(m, L))) break;
+  cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+  if (rc) return rc;
+  if (e != cudaSuccess) return fail(ANVIL_E_CUDA, "graph capture failed: %s", cudaGetErrorString(e));
+  e = cudaGraphInstantiate(&m->graph, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return fail(ANVIL_E_CUDA, "graph instantiate failed: %s", cudaGetErrorString(e));
+  return ANVIL_OK;
+}
+
+static int check_io(const anvil_model *m, const anvil_io *io, int n, const char *what) {
+  for (int i = 0; i < n; ++i)
+    if (io[i].offset > m->arena_bytes || io[i].bytes > m->arena_bytes - io[i].offset)
+      return fail(ANVIL_E_BAD_ARG, "%s %d: [%llu, +%llu) outside the arena", what, i,
+                  (unsigned long long)io[i].offset, (unsigned long long)io[i].bytes);
+  return ANVIL_OK;
+}
+
+extern "C" int anvil_model_enqueue(anvil_model *m, const anvil_io *inputs, int n_inputs, const anvil_io *outputs,
+                                   int n_outputs) {
+  if (!m || n_inputs < 0 || n_outputs < 0 || (n_inputs && !inputs) || (n_outputs && !outputs))
+    return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_enqueue");
+  int rc;
+  if ((rc = check_io(m, inputs, n_inputs, "input")) || (rc = check_io(m, outputs, n_outputs, "output"))) return rc;
+  CK(cudaSetDevice(m->device));
+  cudaStream_t st = m->stream;
+  if ((rc = ensure_graph(m))) return rc;
+  for (int i = 0; i < n_inputs; ++i)
+    CK(cudaMemcpyAsync(static_cast<uint8_t *>(m->arena) + inputs[i].offset, inputs[i].host, inputs[i].bytes,
+                       cudaMemcpyHostToDevice, st));
+  CK(cudaGraphLaunch(m->graph, st));
+  for (int i = 0; i < n_outputs; ++i)
+    CK(cudaMemcpyAsync(outputs[i].host, static_cast<uint8_t *>(m->arena) + outputs[i].offset, outputs[i].bytes,
+                       cudaMemcpyDeviceToHost, st));
+  return ANVIL_OK;
+}
+
+extern "C" int anvil_model_clear_flags(anvil_model *m) {
+  if (!m) return fail(ANVIL_E_BAD_ARG, "model is NULL");
+  CK(cudaSetDevice(m->device));
+  CK(cudaMemsetAsync(m->flags, 0, FLAG_WORDS * sizeof(uint32_t), m->stream));
+  return ANVIL_OK;
+}
+
+extern "C" int anvil_model_wait(anvil_model *m) {
+  if (!m) return fail(ANVIL_E_BAD_ARG, "model is NULL");
+  CK(cudaSetDevice(m->device));
+  uint32_t hflags[FLAG_WORDS];
+  CK(cudaMemcpyAsync(hflags, m->flags, sizeof hflags, cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  return check_flags(m, hflags);
+}
+
 extern "C" int anvil_model_run_device(anvil_model *m, int iters, int use_graph, float *ms) {
   if (!m || iters < 1) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_run_device");
   CK(cudaSetDevice(m->device));
   cudaStream_t st = m->stream;
-  if (use_graph && !m->graph) {
-    cudaGraph_t g;
-    CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    int rc = ANVIL_OK;
-    for (auto &L : m->launches)
-      if ((rc = launch_op(m, L))) break;
-    cudaError_t e = cudaStreamEndCapture(st, &g);
+  if (use_graph) {
+    int rc = ensure_graph(m);
     if (rc) return rc;
-    if (e != cudaSuccess) return fail(ANVIL_E_CUDA, "graph capture failed: %s", cudaGetErrorString(e));
-    e = cudaGraphInstantiate(&m->graph, g, 0);
-    cudaGraphDestroy(g);
-    if (e != cudaSuccess) return fail(ANVIL_E_CUDA, "graph instantiate failed: %s", cudaGetErrorString(e));
   }
   cudaEvent_t e0, e1;
   CK(cudaEventCreate(&e0));

@@ -144,6 +144,19 @@ ANVIL_API int anvil_model_run(anvil_model *m, const anvil_io *inputs, int n_inpu
  * (CUDA events on the model's stream) in *ms. Used by benchmarks to time kernels with inputs already in HBM. */
 ANVIL_API int anvil_model_run_device(anvil_model *m, int iters, int use_graph, float *ms);
 
+/* The run of anvil_model_run split for pipelines over several models (each its own arena and stream): the H2D
+ * copies of `inputs`, the launch chain (one CUDA graph launch, captured on first use) and the D2H copies of
+ * `outputs`, all enqueued on the model's stream, returning without waiting. A batch split into chunks that are
+ * enqueued round-robin on two or more models overlaps one chunk's copies with another chunk's kernels (the host
+ * buffers should be pinned, and must stay valid until anvil_model_wait returns). Device flags persist across
+ * enqueues: anvil_model_clear_flags resets them (stream-ordered) and anvil_model_wait synchronises the stream and
+ * maps any raised flag to its status, as anvil_model_run does. The pipelined form of the reference's
+ * CompiledModel.run (anvil/driver.py:305-322); no separate reference entry point. */
+ANVIL_API int anvil_model_enqueue(anvil_model *m, const anvil_io *inputs, int n_inputs, const anvil_io *outputs,
+                                  int n_outputs);
+ANVIL_API int anvil_model_clear_flags(anvil_model *m);
+ANVIL_API int anvil_model_wait(anvil_model *m);
+
 /* Read/write raw arena bytes (tests and keep="all" readback). */
 ANVIL_API int anvil_model_read(anvil_model *m, uint64_t offset, void *host, uint64_t bytes);
 ANVIL_API int anvil_model_write(anvil_model *m, uint64_t offset, const void *host, uint64_t bytes);

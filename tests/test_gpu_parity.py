@@ -146,6 +146,48 @@ def test_checked_overflow_raises_like_the_oracle():
     assert not ok.ints["y"].any()
 
 
+@pytest.mark.parametrize("pipeline", [2, 4, 12])
+def test_pipelined_run_matches_the_oracle(pipeline):
+    """A batch split into chunks enqueued round-robin on several device models (copies overlapping kernels) gives
+    the oracle's outputs, into fresh arrays and into caller-owned out= buffers."""
+    module, consts, body = _frozen()
+    rng = np.random.default_rng(21)
+    xs = rng.integers(-(1 << 15), 1 << 15, (12,) + np.shape(body["x"]))
+    want = interp.run(module, {"x": xs}, consts, batch=True)
+    cm = anvil.compile(module, consts=consts, params=CudaParams(pipeline=pipeline))
+    assert cm._chunks(12, "outputs", False) == pipeline
+    _check(cm.run(xs, "cuda", quantized=True).ints, want.values, cm.outputs)
+    o = cm.outputs[0]
+    buf = np.zeros((12,) + tuple(cm.meta[o][1]), dtype=np.int16)
+    res = cm.run(xs, "cuda", quantized=True, out={o: buf})
+    assert res.ints[o] is buf and np.array_equal(buf, want.values[o])
+
+
+def test_pipelined_c3_block_matches_oracle():
+    from anvil import workloads as W
+    cm, gen = W.compile_config("c3", params=CudaParams(pipeline=2))
+    xq = cm.quantize_input(gen(2))
+    want = interp.run(cm.module, {cm.inputs[0]: xq}, cm.consts, batch=True)
+    _check(cm.run(xq, "cuda", quantized=True).ints, want.values, cm.outputs)
+
+
+def test_pipelined_checked_overflow_raises():
+    from anvil.ir import GraphBuilder
+    g = GraphBuilder("ovf")
+    x = g.input("x", [4, 32])
+    w = g.const("w", [32, 8])
+    g.output(g.qlinear("y", x, w, 1 << 20, 4))
+    m = g.module()
+    c = {"w": np.full((32, 8), 127)}
+    cm = anvil.compile(m, consts=c, prove=False, params=CudaParams(pipeline=3))
+    xs = np.zeros((6, 4, 32), dtype=np.int64)
+    xs[4] = 127                                      # only the third chunk overflows
+    with pytest.raises(OverflowError):
+        cm.run(xs, "cuda", quantized=True)
+    ok = cm.run(np.zeros((6, 4, 32), dtype=np.int64), "cuda", quantized=True)   # flags were cleared
+    assert not ok.ints["y"].any()
+
+
 def test_embed_index_error():
     from anvil.ir import GraphBuilder
     g = GraphBuilder("emb")
