@@ -28,7 +28,7 @@ import numpy as np
 from .ir import graph as g
 
 BACKENDS = ("cuda",)
-PIPELINE_MODELS = 3          # device models (arenas + streams) a pipelined run rotates over
+PIPELINE_MODELS = 4          # device models (arenas + streams) a pipelined run rotates over
 PIPELINE_TOKENS = 16384      # "auto" pipeline chunk size, in tokens
 
 
@@ -41,10 +41,10 @@ class CudaParams:
               the static overflow proof does not hold for the graph
     fuse      apply launch fusions (LUT epilogues, fused attention); keep="all" runs disable them
     gemm      "auto" | "tc" (tcgen05 wherever the shape allows) | "simt" (CUDA-core kernel everywhere)
-    pipeline  chunks a device's share of a run is split into, so one chunk's host<->device copies overlap another
-              chunk's kernels (chunks go round-robin over PIPELINE_MODELS device models, each with its own arena
-              and stream); "auto" picks chunks of about PIPELINE_TOKENS tokens when that gives at least two equal
-              ones, 1 disables it. keep="all" and timing runs are never split.
+    pipeline  equal chunks a device's share of a run is split into, so one chunk's host<->device copies overlap
+              another chunk's kernels (the chunks go round-robin over PIPELINE_MODELS device models, each with its
+              own arena and stream); "auto": chunks of about PIPELINE_TOKENS tokens; 1 disables it. keep="all" and
+              timing runs are never split.
     """
     devices: tuple = (0,)
     checked: bool | None = None
@@ -194,34 +194,42 @@ class CompiledModel:
     def footprint(self) -> int:
         return self.plan.footprint
 
-    def _pipe_models(self, device: int) -> list:
-        """PIPELINE_MODELS replicas on `device` for chunked runs (constants uploaded once each)."""
+    def _pipe_models(self, device: int, size: int, count: int) -> list:
+        """`count` replicas on `device` prepared for chunks of `size` samples (constants uploaded once each)."""
         from .runtime.cuda import DeviceModel
-        ms = self._pipes.get(device)
-        if ms is None or self._pool_size_at_upload.get(("pipe", device)) != self._pool.size:
-            for m in ms or []:
-                m.close()
-            blob = self._pool.blob()
-            ms = [DeviceModel(device, blob) for _ in range(PIPELINE_MODELS)]
-            self._pipes[device] = ms
+        prog = self.program(size, "outputs")              # lowered first: it may add constants to the pool
+        pipes = self._pipes.setdefault(device, {})
+        if self._pool_size_at_upload.get(("pipe", device)) != self._pool.size:
+            for ms in pipes.values():
+                for m in ms:
+                    m.close()
+            pipes.clear()
             self._pool_size_at_upload[("pipe", device)] = self._pool.size
-        return ms
+        ms = pipes.setdefault(size, [])
+        while len(ms) < count:
+            ms.append(DeviceModel(device, self._pool.blob()))
+        for m in ms[:count]:
+            if m.prepared_key != (size, "outputs"):
+                m.prepare(prog.ops, prog.plan.arena, key=(size, "outputs"))
+        return ms[:count]
 
-    def _chunks(self, b: int, keep: str, timing: bool) -> int:
-        """How many equal chunks a shard of b samples runs in (1: one launch chain)."""
+    def _chunk_plan(self, b: int, keep: str, timing: bool) -> list:
+        """Sample counts of the chunks a shard of b samples runs as ([b]: one launch chain)."""
         if keep != "outputs" or timing or b < 2:
-            return 1
+            return [b]
         if self.params.pipeline != "auto":
             n = min(int(self.params.pipeline), b)
             while b % n:
                 n -= 1
-            return n
-        tokens = b * max(1, self._tokens_per_sample())
-        want = max(1, round(tokens / PIPELINE_TOKENS))
-        for n in sorted(range(2, b + 1), key=lambda k: (abs(k - want), k)):
-            if b % n == 0 and n <= want * 2:
-                return n
-        return 1
+            return [b // n] * n
+        per = max(1, PIPELINE_TOKENS // max(1, self._tokens_per_sample()))       # samples per chunk
+        want = max(1, round(b / per))
+        divs = [n for n in range(1, b + 1) if b % n == 0]
+        n = min(divs, key=lambda k: (abs(k - want), k))
+        return [b // n] * n
+
+    def _chunks(self, b: int, keep: str, timing: bool) -> int:
+        return len(self._chunk_plan(b, keep, timing))
 
     def _tokens_per_sample(self) -> int:
         """Rows of the first input per sample (sequence length for (T, d) or (T,) inputs)."""
@@ -405,9 +413,9 @@ class CompiledModel:
         return ints, results[0][1], [(d, hi - lo) for d, lo, hi in shards]
 
     def _run_shard(self, device, bound, b, keep, timing, out=None):
-        n = self._chunks(b, keep, timing)
-        if n > 1 and self._pipelinable(self.program(b // n, keep)):
-            return self._run_pipelined(device, bound, b, n, out)
+        plan = self._chunk_plan(b, keep, timing)
+        if len(plan) > 1 and all(self._pipelinable(self.program(c, keep)) for c in set(plan)):
+            return self._run_pipelined(device, bound, b, plan, out)
         prog = self.program(b, keep)
         dm = self._device_model(device)
         if dm.prepared_key != (b, keep):
@@ -450,34 +458,40 @@ class CompiledModel:
                 return False
         return True
 
-    def _run_pipelined(self, device, bound, b, n, out=None):
-        """The shard as n equal chunks enqueued round-robin on PIPELINE_MODELS device models: while one chunk's
-        kernels run, the next chunk's inputs are copied in and the previous chunk's outputs copied out (each model
-        has its own stream and arena; the copies go straight between the caller's arrays and the device)."""
+    def _run_pipelined(self, device, bound, b, plan, out=None):
+        """The shard as chunks of plan[i] samples, each enqueued on a device model prepared for its size: equal-size
+        chunks rotate over PIPELINE_MODELS models (own stream and arena each), so while one chunk's kernels run the
+        next chunk's inputs are copied in and the previous chunk's outputs copied out, straight between the
+        caller's arrays and the device."""
         from .runtime.program import NP
-        cb = b // n
-        prog = self.program(cb, "outputs")
-        models = self._pipe_models(device)
-        for dm in models:
-            if dm.prepared_key != (cb, "outputs"):
-                dm.prepare(prog.ops, prog.plan.arena, key=(cb, "outputs"))
-        ins = {sym: np.ascontiguousarray(bound[sym], dtype=NP[dtype]) for sym, (_, _, dtype) in prog.inputs.items()}
-        want = self._readable(prog, "outputs")
+        sizes = sorted(set(plan))
+        counts = {c: min(PIPELINE_MODELS, plan.count(c)) for c in sizes}
+        models = {c: self._pipe_models(device, c, counts[c]) for c in sizes}
+        prog0 = self.program(plan[0], "outputs")
+        ins = {sym: np.ascontiguousarray(bound[sym], dtype=NP[dtype]) for sym, (_, _, dtype) in prog0.inputs.items()}
         res = {}
-        for sym, v in want.items():
-            if out and sym in out and v.contiguous and out[sym].nbytes == n * prog.buffers[v.root]:
+        for sym in self._readable(prog0, "outputs"):
+            full = (b,) + tuple(self.meta[sym][1])
+            if out and sym in out:
                 res[sym] = out[sym]
             else:
-                res[sym] = np.empty((b,) + tuple(self.meta[sym][1]), dtype=NP[self.meta[sym][2]])
-        used = models[:min(n, len(models))]
+                res[sym] = np.empty(full, dtype=NP[self.meta[sym][2]])
+        used = [m for c in sizes for m in models[c]]
         for dm in used:
             dm.clear_flags()
+        turn = {c: 0 for c in sizes}
         try:
-            for i in range(n):
-                lo, hi = i * cb, (i + 1) * cb
-                dm = used[i % len(used)]
+            lo, prev = 0, None
+            for c in plan:
+                prog = self.program(c, "outputs")
+                dm = models[c][turn[c] % counts[c]]
+                turn[c] += 1
+                hi = lo + c
                 dm.enqueue([(off, ins[sym][lo:hi]) for sym, (off, _, _) in prog.inputs.items()],
-                           [(prog.plan.addresses[v.root], res[sym][lo:hi]) for sym, v in want.items()])
+                           [(prog.plan.addresses[v.root], res[sym][lo:hi])
+                            for sym, v in self._readable(prog, "outputs").items()],
+                           after=prev if prev is not dm else None)
+                lo, prev = hi, dm
         finally:
             errs = []
             for dm in used:
@@ -487,12 +501,7 @@ class CompiledModel:
                     errs.append(e)
             if errs:
                 raise errs[0]
-        ints = {}
-        for sym in want:
-            ints[sym] = res[sym]
-            if out and sym in out and res[sym] is not out[sym]:
-                out[sym][...] = res[sym]
-                ints[sym] = out[sym]
+        ints = dict(res)
         for sym in self.inputs:
             ints.setdefault(sym, bound[sym])
         return ints, None

@@ -71,7 +71,7 @@ def load_library(path: str | os.PathLike | None = None):
             "anvil_model_run": ([vp, ctypes.POINTER(AnvilIO), i32, ctypes.POINTER(AnvilIO), i32,
                                  ctypes.POINTER(ctypes.c_float)], i32),
             "anvil_model_run_device": ([vp, i32, i32, ctypes.POINTER(ctypes.c_float)], i32),
-            "anvil_model_enqueue": ([vp, ctypes.POINTER(AnvilIO), i32, ctypes.POINTER(AnvilIO), i32], i32),
+            "anvil_model_enqueue": ([vp, ctypes.POINTER(AnvilIO), i32, ctypes.POINTER(AnvilIO), i32, vp], i32),
             "anvil_model_clear_flags": ([vp], i32),
             "anvil_model_wait": ([vp], i32),
             "anvil_model_read": ([vp, u64, vp, u64], i32),
@@ -134,12 +134,15 @@ class DeviceModel:
         check(self.lib.anvil_model_run(self._h, ins, len(inputs), outs, len(outputs), us), "anvil_model_run")
         return list(us)[: self.n_ops] if timing else None
 
-    def enqueue(self, inputs: list[tuple[int, np.ndarray]], outputs: list[tuple[int, np.ndarray]]):
-        """anvil_model_enqueue: copies in, the launch chain, copies out, on this model's stream, without waiting.
-        The host arrays must stay alive (and unmodified) until wait() returns."""
+    def enqueue(self, inputs: list[tuple[int, np.ndarray]], outputs: list[tuple[int, np.ndarray]],
+                after: "DeviceModel | None" = None):
+        """anvil_model_enqueue: copies in, the launch chain, copies out, on this model's stream, without waiting;
+        with `after`, chained behind that model's latest copies in and launch chain (a pipeline stage). The host
+        arrays must stay alive (and unmodified) until wait() returns."""
         ins = (AnvilIO * max(1, len(inputs)))(*[AnvilIO(o, a.ctypes.data, a.nbytes) for o, a in inputs])
         outs = (AnvilIO * max(1, len(outputs)))(*[AnvilIO(o, a.ctypes.data, a.nbytes) for o, a in outputs])
-        check(self.lib.anvil_model_enqueue(self._h, ins, len(inputs), outs, len(outputs)), "anvil_model_enqueue")
+        check(self.lib.anvil_model_enqueue(self._h, ins, len(inputs), outs, len(outputs),
+                                           after._h if after is not None else None), "anvil_model_enqueue")
 
     def clear_flags(self):
         check(self.lib.anvil_model_clear_flags(self._h), "anvil_model_clear_flags")

@@ -130,6 +130,8 @@ struct anvil_model {
   std::vector<Launch> launches;
   cudaGraphExec_t graph = nullptr;
   std::vector<cudaEvent_t> events;
+  // pipelined enqueues: recorded after this model's last input copies and after its last launch chain
+  cudaEvent_t ev_in = nullptr, ev_run = nullptr;
 };
 
 extern "C" int anvil_device_count(int *count) {
@@ -219,6 +221,8 @@ extern "C" void anvil_model_free(anvil_model *m) {
   if (m->stream) cudaStreamSynchronize(m->stream);
   if (m->graph) cudaGraphExecDestroy(m->graph);
   for (auto e : m->events) cudaEventDestroy(e);
+  if (m->ev_in) cudaEventDestroy(m->ev_in);
+  if (m->ev_run) cudaEventDestroy(m->ev_run);
   if (m->arena) cudaFree(m->arena);
   if (m->consts) cudaFree(m->consts);
   if (m->flags) cudaFree(m->flags);
@@ -753,18 +757,28 @@ static int check_io(const anvil_model *m, const anvil_io *io, int n, const char 
 }
 
 extern "C" int anvil_model_enqueue(anvil_model *m, const anvil_io *inputs, int n_inputs, const anvil_io *outputs,
-                                   int n_outputs) {
+                                   int n_outputs, anvil_model *after) {
   if (!m || n_inputs < 0 || n_outputs < 0 || (n_inputs && !inputs) || (n_outputs && !outputs))
     return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_enqueue");
+  if (after && (after == m || after->device != m->device))
+    return fail(ANVIL_E_BAD_ARG, "anvil_model_enqueue: `after` must be another model on the same device");
   int rc;
   if ((rc = check_io(m, inputs, n_inputs, "input")) || (rc = check_io(m, outputs, n_outputs, "output"))) return rc;
   CK(cudaSetDevice(m->device));
   cudaStream_t st = m->stream;
   if ((rc = ensure_graph(m))) return rc;
+  if (!m->ev_in) CK(cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming));
+  if (!m->ev_run) CK(cudaEventCreateWithFlags(&m->ev_run, cudaEventDisableTiming));
+  // chained behind `after`: the copies in start once its copies in are done (one chunk at a time at full bus
+  // speed), the launch chain once its chain is done (one chunk's kernels on the SMs at a time)
+  if (after && after->ev_in) CK(cudaStreamWaitEvent(st, after->ev_in, 0));
   for (int i = 0; i < n_inputs; ++i)
     CK(cudaMemcpyAsync(static_cast<uint8_t *>(m->arena) + inputs[i].offset, inputs[i].host, inputs[i].bytes,
                        cudaMemcpyHostToDevice, st));
+  CK(cudaEventRecord(m->ev_in, st));
+  if (after && after->ev_run) CK(cudaStreamWaitEvent(st, after->ev_run, 0));
   CK(cudaGraphLaunch(m->graph, st));
+  CK(cudaEventRecord(m->ev_run, st));
   for (int i = 0; i < n_outputs; ++i)
     CK(cudaMemcpyAsync(outputs[i].host, static_cast<uint8_t *>(m->arena) + outputs[i].offset, outputs[i].bytes,
                        cudaMemcpyDeviceToHost, st));

@@ -163,6 +163,20 @@ def test_pipelined_run_matches_the_oracle(pipeline):
     assert res.ints[o] is buf and np.array_equal(buf, want.values[o])
 
 
+def test_auto_pipeline_matches_the_oracle(monkeypatch):
+    """The "auto" plan (chunks of about PIPELINE_TOKENS tokens; more chunks than device models, so the models are
+    reused within one run) gives the oracle's outputs."""
+    import anvil.driver as D
+    monkeypatch.setattr(D, "PIPELINE_TOKENS", 2 * 16)            # 2 samples of T = 16 per chunk
+    module, consts, body = _frozen()
+    rng = np.random.default_rng(22)
+    xs = rng.integers(-(1 << 15), 1 << 15, (14,) + np.shape(body["x"]))
+    want = interp.run(module, {"x": xs}, consts, batch=True)
+    cm = anvil.compile(module, consts=consts)
+    assert cm._chunk_plan(14, "outputs", False) == [2] * 7
+    _check(cm.run(xs, "cuda", quantized=True).ints, want.values, cm.outputs)
+
+
 def test_pipelined_c3_block_matches_oracle():
     from anvil import workloads as W
     cm, gen = W.compile_config("c3", params=CudaParams(pipeline=2))
