@@ -625,7 +625,9 @@ def lower_program(module, consts: dict, pool: ConstPool, batch: int, keep="outpu
         for w in d.writes:
             defs.setdefault(w, i)
     input_bufs = set(L.inputs.values())
-    keep_roots = {v.root for _, v in outs if not v.const}
+    # the graph inputs stay live through the whole chain (never reused), so a device-resident replay of the
+    # chain (anvil_model_run_device, graph replays) reads the same inputs every time
+    keep_roots = {v.root for _, v in outs if not v.const} | input_bufs
     if keep == "all":
         keep_roots |= {v.root for v in views.values()}
     sizes = {b: n for b, n in L.bufs.items() if b in defs or b in input_bufs}

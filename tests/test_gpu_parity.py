@@ -177,6 +177,27 @@ def test_auto_pipeline_matches_the_oracle(monkeypatch):
     _check(cm.run(xs, "cuda", quantized=True).ints, want.values, cm.outputs)
 
 
+def test_device_replays_keep_the_inputs():
+    """anvil_model_run_device replays the chain on the arena (the bench's device-timed loop): the graph inputs are
+    never reused by the memory plan, so after several replays the outputs still equal the oracle's (config c2,
+    whose embedding would raise an index error on overwritten token ids)."""
+    from anvil import workloads as W
+    cm, gen = W.compile_config("c2")
+    ids = np.asarray(gen(4))
+    want = interp.run(cm.module, {cm.inputs[0]: ids}, cm.consts, batch=True)
+    prog = cm.program(4)
+    dm = cm._device_model(0)
+    dm.prepare(prog.ops, prog.plan.arena, key=(4, "outputs"))
+    dm.write(prog.inputs[cm.inputs[0]][0], np.ascontiguousarray(ids, dtype=np.int32))
+    dm.run_device(3, use_graph=True)
+    for sym, v in prog.outputs:
+        if sym is None or v.const:
+            continue
+        from anvil.driver import _apply_view
+        buf = dm.read(prog.plan.addresses[v.root], np.empty(prog.buffers[v.root], dtype=np.uint8))
+        assert np.array_equal(_apply_view(buf, v), want.values[sym]), sym
+
+
 def test_pipelined_c3_block_matches_oracle():
     from anvil import workloads as W
     cm, gen = W.compile_config("c3", params=CudaParams(pipeline=2))
