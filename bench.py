@@ -241,6 +241,7 @@ def run_ours(args):
     ws, rank, local = _dist()
     if ws > 1:
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")    # stdout carries only the JSON line
     torch.cuda.set_device(local)
     dist = _pg(ws, "nccl")
     cfg = args.config
