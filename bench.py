@@ -53,6 +53,34 @@ def _peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+INT8_SPEC_TOPS = 4500.0       # B200 dense int8 tensor peak, NVIDIA's nominal figure (the 9 POPS one is 2:4 sparse)
+
+
+def int8_peak_measured(device=None):
+    """This GPU's dense int8 GEMM rate, measured here: torch._int_mm (cuBLASLt int8 -> int32) on 8192^3, best of 10
+    launches timed with CUDA events. None when the library GEMM is unavailable."""
+    import torch
+    try:
+        n = 8192
+        g = torch.Generator(device="cuda").manual_seed(0)
+        a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda", generator=g)
+        b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda", generator=g).t().contiguous().t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b
+        return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+    except Exception:
+        return None
+
+
 class ClockSampler:
     """SM clock and throttle reasons sampled during the timed region: NVML every ~5 ms on a background thread
     (the recipe's nvidia-smi clocks line, at a rate a millisecond-scale region can catch), nvidia-smi as fallback."""
@@ -297,7 +325,8 @@ def run_ours(args):
         kus2 = dm.run([(off, xin)], [], timing=True)
         kus = [min(a, b) for a, b in zip(kus, kus2)]
     hbm, bf16, src = _peaks()
-    roofs = _rooflines(prog, kus, hbm, bf16, src, C)
+    i8peak = int8_peak_measured()
+    roofs = _rooflines(prog, kus, hbm, bf16, src, C, i8peak)
     by_kind = {k: round(r["total_us"], 2) for k, r in roofs.items()}
     dominant = max(roofs, key=lambda k: roofs[k]["total_us"])
     roofline = {k: v for k, v in roofs[dominant].items() if k != "total_us"}
@@ -335,7 +364,7 @@ def run_ours(args):
             "gpu_launches": sum(1 for d in prog.devops if d.kind != C.OP_COPY) * args.steps,
             "clocks": clk.summary()}
     if rank == 0 and ws == 1 and not args.no_sweep:
-        line["gemm_sweep_c4"] = gemm_sweep(2 * bf16)
+        line["gemm_sweep_c4"] = gemm_sweep(i8peak or 2 * bf16)
     if rank == 0 and ws == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(cfg, cm, gen)
     if rank == 0:
@@ -346,9 +375,11 @@ def run_ours(args):
     return 0
 
 
-def _rooflines(prog, kus, hbm, bf16, src, C):
+def _rooflines(prog, kus, hbm, bf16, src, C, i8peak=None):
     """Per kernel family: algorithmic ops (tensor-bound families) or bytes (HBM-bound) per launch over the average
-    CUDA-event launch time, against 2 x measured bf16 (dense int8) or the measured copy bandwidth."""
+    CUDA-event launch time. Tensor families are measured against this GPU's int8 GEMM rate measured in the same run
+    (torch._int_mm, 8192^3) when it could be, with the fractions of 2 x the measured dense bf16 rate and of the 4.5
+    POPS dense-int8 spec alongside; HBM families against the measured copy bandwidth."""
     fam = {}
     for d, u in zip(prog.devops, kus):
         k = C.KIND_NAMES[d.kind]
@@ -360,10 +391,15 @@ def _rooflines(prog, kus, hbm, bf16, src, C):
     out = {}
     for k, f in fam.items():
         avg = f["us"] / f["n"]
+        extra = {}
         if f["ops"]:
             ach = f["ops"] / f["n"] / (avg * 1e-6) / 1e12
-            peak, unit, bound = 2 * bf16, "TOP/s", "tensor"
-            ps = f"2 x {src} bf16_tflops {bf16} (dense int8 = 2 x dense bf16 on B200)"
+            unit, bound = "TOP/s", "tensor"
+            if i8peak:
+                peak, ps = i8peak, "int8 GEMM rate measured in this run (torch._int_mm, 8192^3, best of 10)"
+            else:
+                peak, ps = 2 * bf16, f"2 x {src} bf16_tflops {bf16} (dense int8 = 2 x dense bf16 on B200)"
+            extra = {"frac_of_2x_bf16": ach / (2 * bf16), "frac_of_int8_spec": ach / INT8_SPEC_TOPS}
             per = {"ops_per_launch": f["ops"] / f["n"]}
         else:
             ach = f["bytes"] / f["n"] / (avg * 1e-6) / 1e9
@@ -371,7 +407,8 @@ def _rooflines(prog, kus, hbm, bf16, src, C):
             ps = f"{src} hbm_gbs {hbm}"
             per = {"bytes_per_launch": f["bytes"] / f["n"]}
         out[k] = {"kernel": k, "bound": bound, "achieved": ach, "peak": peak, "unit": unit, "frac": ach / peak,
-                  "peak_source": ps, "avg_launch_us": avg, "launches_per_step": f["n"], "total_us": f["us"], **per}
+                  **extra, "peak_source": ps, "avg_launch_us": avg, "launches_per_step": f["n"],
+                  "total_us": f["us"], **per}
     return out
 
 
