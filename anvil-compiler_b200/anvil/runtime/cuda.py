@@ -29,7 +29,7 @@ KIND_NAMES = {OP_GEMM: "gemm", OP_LUT: "lut", OP_LUT_MUL: "lut_mul", OP_ADD_REQU
 
 EXPORTS = ("anvil_abi_version", "anvil_last_error", "anvil_device_count", "anvil_cuda_init", "anvil_model_create",
            "anvil_model_prepare", "anvil_model_run", "anvil_model_enqueue", "anvil_model_clear_flags",
-           "anvil_model_wait", "anvil_model_run_device", "anvil_model_read",
+           "anvil_model_wait", "anvil_model_selftest_timeout", "anvil_model_run_device", "anvil_model_read",
            "anvil_model_write", "anvil_model_arena", "anvil_model_free", "anvil_gemm_requant")
 
 
@@ -74,6 +74,7 @@ def load_library(path: str | os.PathLike | None = None):
             "anvil_model_enqueue": ([vp, ctypes.POINTER(AnvilIO), i32, ctypes.POINTER(AnvilIO), i32, vp], i32),
             "anvil_model_clear_flags": ([vp], i32),
             "anvil_model_wait": ([vp], i32),
+            "anvil_model_selftest_timeout": ([vp, u64], i32),
             "anvil_model_read": ([vp, u64, vp, u64], i32),
             "anvil_model_write": ([vp, u64, vp, u64], i32),
             "anvil_model_arena": ([vp, ctypes.POINTER(u64), ctypes.POINTER(u64)], i32),
@@ -150,6 +151,10 @@ class DeviceModel:
     def wait(self):
         """Synchronise this model's stream and raise if a device check fired since clear_flags()."""
         check(self.lib.anvil_model_wait(self._h), "anvil_model_wait")
+
+    def selftest_timeout(self, wait_ns: int):
+        """Run the device wait-bound self-test: raises TimeoutError after about wait_ns (the expected outcome)."""
+        check(self.lib.anvil_model_selftest_timeout(self._h, int(wait_ns)), "anvil_model_selftest_timeout")
 
     def run_device(self, iters: int = 1, use_graph: bool = True) -> float:
         ms = ctypes.c_float(0)

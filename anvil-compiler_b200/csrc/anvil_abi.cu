@@ -687,6 +687,37 @@ static int check_flags(anvil_model *m, const uint32_t *h) {
   return ANVIL_OK;
 }
 
+// Self-test of the device wait bound: two warps wait on an mbarrier that nothing arrives on, through the same
+// bounded wait the kernels use (here with the caller's limit); the wait gives up, raises the timeout flag and sets
+// the block's abort word, so the other warp gives up too, and the kernel returns.
+__global__ void __launch_bounds__(64) selftest_wait_kernel(uint32_t *flags, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_word;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_word = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0)
+    mbar_wait_for(&bar, 0, reinterpret_cast<volatile int *>(&abort_word), flags, 0, limit_ns);
+  __syncwarp();
+}
+
+extern "C" int anvil_model_selftest_timeout(anvil_model *m, uint64_t wait_ns) {
+  if (!m || wait_ns == 0 || wait_ns > ANVIL_DEV_WAIT_NS)
+    return fail(ANVIL_E_BAD_ARG, "anvil_model_selftest_timeout: wait_ns must be in (0, %llu]",
+                (unsigned long long)ANVIL_DEV_WAIT_NS);
+  CK(cudaSetDevice(m->device));
+  CK(cudaMemsetAsync(m->flags, 0, FLAG_WORDS * sizeof(uint32_t), m->stream));
+  selftest_wait_kernel<<<1, 64, 0, m->stream>>>(m->flags, wait_ns);
+  CK(cudaGetLastError());
+  uint32_t hflags[FLAG_WORDS];
+  CK(cudaMemcpyAsync(hflags, m->flags, sizeof hflags, cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  return check_flags(m, hflags);
+}
+
 extern "C" int anvil_model_run(anvil_model *m, const anvil_io *inputs, int n_inputs, const anvil_io *outputs,
                                int n_outputs, float *kernel_us) {
   if (!m) return fail(ANVIL_E_BAD_ARG, "model is NULL");

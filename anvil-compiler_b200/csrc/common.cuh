@@ -130,8 +130,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Bounded wait for the phase with `parity` to complete. Returns false (after setting *abort and the timeout flag)
 // if the wait gives up, or immediately if another role of the CTA already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort, uint32_t *flags,
-                                          int op_index) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, volatile int *abort, uint32_t *flags,
+                                              int op_index, uint64_t limit_ns) {
   uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   uint64_t t0 = globaltimer();
@@ -139,13 +139,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     if (mbar_try_wait(a, parity)) return true;
     if ((it & 255u) == 0) {
       if (*abort) return false;
-      if (globaltimer() - t0 > ANVIL_DEV_WAIT_NS) {
+      if (globaltimer() - t0 > limit_ns) {
         *abort = 1;
         raise_flag(flags, FLAG_TIMEOUT, op_index);
         return false;
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort, uint32_t *flags,
+                                          int op_index) {
+  return mbar_wait_for(bar, parity, abort, flags, op_index, ANVIL_DEV_WAIT_NS);
 }
 
 // mbarrier.try_wait with a suspend-time hint: the thread sleeps until the phase completes or `hint_ns` passes.

@@ -160,6 +160,13 @@ ANVIL_API int anvil_model_enqueue(anvil_model *m, const anvil_io *inputs, int n_
 ANVIL_API int anvil_model_clear_flags(anvil_model *m);
 ANVIL_API int anvil_model_wait(anvil_model *m);
 
+/* Self-test of the device-side wait bound every kernel relies on: launches one block whose warps wait, through
+ * the same bounded mbarrier wait, on a barrier nothing arrives on, with a limit of `wait_ns` (at most the kernels'
+ * own 2 s). The wait gives up and raises the timeout flag, so the call returns ANVIL_E_TIMEOUT after about wait_ns,
+ * and the model (its stream and context) stays usable. No reference counterpart: the reference's analogue is the
+ * simulators' timeout_cycles (anvil/runtime/api.py:104-124). */
+ANVIL_API int anvil_model_selftest_timeout(anvil_model *m, uint64_t wait_ns);
+
 /* Read/write raw arena bytes (tests and keep="all" readback). */
 ANVIL_API int anvil_model_read(anvil_model *m, uint64_t offset, void *host, uint64_t bytes);
 ANVIL_API int anvil_model_write(anvil_model *m, uint64_t offset, const void *host, uint64_t bytes);

@@ -223,6 +223,24 @@ def test_pipelined_checked_overflow_raises():
     assert not ok.ints["y"].any()
 
 
+def test_device_wait_bound_times_out_and_the_context_survives():
+    """The bounded mbarrier wait every tcgen05 kernel uses gives up after its limit on a barrier nothing arrives on:
+    the self-test returns TimeoutError after about the limit, and the same model then runs a graph bit-exactly."""
+    import time
+    module, consts, body = _frozen()
+    cm = anvil.compile(module, consts=consts)
+    xs = np.asarray(body["x"])[None]
+    cm.run(xs, "cuda", quantized=True)
+    dm = cm._device_model(0)
+    t = time.perf_counter()
+    with pytest.raises(TimeoutError):
+        dm.selftest_timeout(50_000_000)                     # 50 ms
+    dt = time.perf_counter() - t
+    assert 0.04 < dt < 1.5, dt
+    want = interp.run(module, {"x": xs}, consts, batch=True)
+    _check(cm.run(xs, "cuda", quantized=True).ints, want.values, cm.outputs)
+
+
 def test_embed_index_error():
     from anvil.ir import GraphBuilder
     g = GraphBuilder("emb")
