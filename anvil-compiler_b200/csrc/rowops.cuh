@@ -276,12 +276,13 @@ __device__ __forceinline__ int sbyte_prmt(uint32_t w, int q) {
 // sum of squares is sum(x^2) - 2 mean sum(x) + d mean^2, the same integer. The output multiplies (x - mean) * w by
 // r * M, equal mod 2^32 to ((x - mean) * w * r) * M, and exact because the proof bounds the true value.
 template <int NV8>
-__global__ void __launch_bounds__(256) norm_row_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w,
+__global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 3 : NV8 == 4 ? 2 : 1) norm_row_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w,
                                                        const int32_t *__restrict__ lut,
                                                        const int8_t *__restrict__ bias, int8_t *__restrict__ out,
                                                        int64_t rows, int n, int m, int s, int c, int e, int center) {
   constexpr int d = 256 * NV8;
   const int lane = threadIdx.x & 31;
+  const int ln = 32 - __clz(n);
   int wr[8 * NV8], br[8 * NV8];
 #pragma unroll
   for (int v = 0; v < NV8; ++v) {
@@ -316,17 +317,13 @@ __global__ void __launch_bounds__(256) norm_row_kernel(const int8_t *__restrict_
       sxx = __dp4a((int)xv[v].x, (int)xv[v].x, sxx);
       sxx = __dp4a((int)xv[v].y, (int)xv[v].y, sxx);
     }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, o);
+    sx = __reduce_add_sync(0xffffffffu, sx);
     int mean = 0;
-    if (center) {
-      const int num = sx + d / 2;                          // floor division by d > 0
-      mean = num >= 0 ? num / d : -((-num + d - 1) / d);
-    }
+    // floor((sx + d/2) / d): |sx| <= 128 d, so the offset of 128 d makes the dividend positive
+    if (center) mean = (int)((unsigned)(sx + d / 2 + 128 * d) / (unsigned)d) - 128;
     int ss;
     if (c == 0) {
-#pragma unroll
-      for (int o = 16; o; o >>= 1) sxx += __shfl_xor_sync(0xffffffffu, sxx, o);
+      sxx = __reduce_add_sync(0xffffffffu, sxx);
       ss = sxx - 2 * mean * sx + d * mean * mean;
     } else {
       ss = 0;
@@ -341,9 +338,13 @@ __global__ void __launch_bounds__(256) norm_row_kernel(const int8_t *__restrict_
       for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     }
     ss += e;
-    int idx = ss, k = 0;
-    while (idx >= n) { idx >>= 2; ++k; }
-    const int rm = lut[idx] * m;
+    int k = 0;
+    if (ss >= n) {
+      // the smallest k with (ss >> 2k) < n: bit lengths give it to within one step
+      const int ka = max(0, (32 - __clz(ss) - ln + 1) >> 1);
+      k = ka + ((ss >> (2 * ka)) >= n);
+    }
+    const int rm = lut[ss >> (2 * k)] * m;
     const int sh = s + k;
     const int rnd = sh ? 1 << (sh - 1) : 0;
     uint2 *orow = reinterpret_cast<uint2 *>(out + row * d);
