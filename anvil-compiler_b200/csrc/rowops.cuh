@@ -270,45 +270,46 @@ __device__ __forceinline__ int sbyte_prmt(uint32_t w, int q) {
 }
 
 // norm_vec for rows of d = 256 * NV8 int8 values (unchecked, static int32 proof). One warp per row, every lane
-// NV8 8-byte vectors (lane + 32 v); the weights and bias sign-extended into registers once per thread; the next
-// row's vectors loaded before the current row is computed (two rows in flight per warp). Row statistics come from
-// dp4a (sum and sum of squares, exact in int32 for d <= 2048); with no per-element shift (c == 0) the centered
-// sum of squares is sum(x^2) - 2 mean sum(x) + d mean^2, the same integer. The output multiplies (x - mean) * w by
-// r * M, equal mod 2^32 to ((x - mean) * w * r) * M, and exact because the proof bounds the true value.
+// NV8 8-byte vectors (lane + 32 v); the weights (as dp2a byte pairs) and the bias held in registers once per
+// thread; the next row's vectors loaded before the current row is computed (two rows in flight per warp). Row
+// statistics come from dp4a and redux.sync (sum and sum of squares, exact in int32 for d <= 2048); with no
+// per-element shift (c == 0) the centered sum of squares is sum(x^2) - 2 mean sum(x) + d mean^2, the same integer.
+// Each output element takes one byte permute ({x_q, -mean} as 16-bit halves) and one dp2a for (x_q - mean) * w_q;
+// that times r * M is equal mod 2^32 to ((x - mean) * w * r) * M, exact because the proof bounds the true value.
+// The launch bounds keep the register budget that gives 5/4/3/2 resident blocks for 256/512/768/1024-wide rows.
 template <int NV8>
-__global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 3 : NV8 == 4 ? 2 : 1) norm_row_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w,
+__global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 3 : NV8 == 4 ? 2 : 1)
+    norm_row_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w,
                                                        const int32_t *__restrict__ lut,
                                                        const int8_t *__restrict__ bias, int8_t *__restrict__ out,
                                                        int64_t rows, int n, int m, int s, int c, int e, int center) {
   constexpr int d = 256 * NV8;
   const int lane = threadIdx.x & 31;
   const int ln = 32 - __clz(n);
-  int wr[8 * NV8], br[8 * NV8];
+  uint32_t wp[4 * NV8];                            // weight pairs {w_2j, w_2j, w_2j+1, w_2j+1} for dp2a
+  int br[8 * NV8];
 #pragma unroll
   for (int v = 0; v < NV8; ++v) {
     const uint2 w2 = reinterpret_cast<const uint2 *>(w)[lane + 32 * v];
     const uint2 b2 = bias ? reinterpret_cast<const uint2 *>(bias)[lane + 32 * v] : make_uint2(0, 0);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      wr[8 * v + q] = sbyte_prmt(q < 4 ? w2.x : w2.y, q & 3);
-      br[8 * v + q] = sbyte_prmt(q < 4 ? b2.x : b2.y, q & 3);
+    for (int q = 0; q < 8; ++q) br[8 * v + q] = sbyte_prmt(q < 4 ? b2.x : b2.y, q & 3);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t b0 = (2 * j) & 3, b1 = b0 + 1;
+      wp[4 * v + j] = __byte_perm(j < 2 ? w2.x : w2.y, 0u, b0 | b0 << 4 | b1 << 8 | b1 << 12);
     }
   }
   const int rc = c ? 1 << (c - 1) : 0;
   const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  uint2 xv[NV8];
-  if (warp < rows) {
-#pragma unroll
-    for (int v = 0; v < NV8; ++v) xv[v] = reinterpret_cast<const uint2 *>(x + warp * d)[lane + 32 * v];
-  }
-  for (int64_t row = warp; row < rows; row += nwarps) {
-    uint2 xn[NV8];
-    const int64_t nrow = row + nwarps;
-    if (nrow < rows) {
-#pragma unroll
-      for (int v = 0; v < NV8; ++v) xn[v] = reinterpret_cast<const uint2 *>(x + nrow * d)[lane + 32 * v];
-    }
+  if (warp >= rows) return;
+  const int nr = (int)((rows - 1 - warp) / nwarps) + 1;       // rows of this warp: warp, warp + nwarps, ...
+  const int64_t step = nwarps * (d / 8);                        // one warp-stride of rows, in 8-byte vectors
+  const uint2 *xp = reinterpret_cast<const uint2 *>(x + warp * d) + lane;
+  uint2 *op = reinterpret_cast<uint2 *>(out + warp * d) + lane;
+
+  auto row_out = [&](const uint2 (&xv)[NV8], uint2 *orow) {
     int sx = 0, sxx = 0;
 #pragma unroll
     for (int v = 0; v < NV8; ++v) {
@@ -334,8 +335,7 @@ __global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 
           const int xc = sbyte_prmt(q < 4 ? xv[v].x : xv[v].y, q & 3) - mean;
           ss += (xc * xc + rc) >> c;
         }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      ss = __reduce_add_sync(0xffffffffu, ss);
     }
     ss += e;
     int k = 0;
@@ -347,19 +347,41 @@ __global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 
     const int rm = lut[ss >> (2 * k)] * m;
     const int sh = s + k;
     const int rnd = sh ? 1 << (sh - 1) : 0;
-    uint2 *orow = reinterpret_cast<uint2 *>(out + row * d);
+    const uint32_t nm = (uint32_t)(-mean) << 16;
 #pragma unroll
     for (int v = 0; v < NV8; ++v) {
       int y[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        const int xc = sbyte_prmt(q < 4 ? xv[v].x : xv[v].y, q & 3) - mean;
-        y[q] = (((xc * wr[8 * v + q]) * rm + rnd) >> sh) + br[8 * v + q];
+        // {x_q sign-extended, -mean} as two 16-bit halves, so one dp2a gives (x_q - mean) * w_q
+        int a;
+        asm("prmt.b32 %0, %1, %2, %3;" : "=r"(a) : "r"(q < 4 ? xv[v].x : xv[v].y), "r"(nm),
+            "r"((uint32_t)(q & 3) | (uint32_t)((q & 3) | 8) << 4 | 0x7600u));
+        const int t = (q & 1) ? __dp2a_hi(a, (int)wp[4 * v + q / 2], 0) : __dp2a_lo(a, (int)wp[4 * v + q / 2], 0);
+        y[q] = ((t * rm + rnd) >> sh) + br[8 * v + q];
       }
-      orow[lane + 32 * v] = make_uint2(pack4_sat_s8(y[0], y[1], y[2], y[3]), pack4_sat_s8(y[4], y[5], y[6], y[7]));
+      orow[32 * v] = make_uint2(pack4_sat_s8(y[0], y[1], y[2], y[3]), pack4_sat_s8(y[4], y[5], y[6], y[7]));
     }
+  };
+
+  // two row buffers in turn: the next row's vectors are in flight while the current row is computed
+  uint2 xa[NV8], xb[NV8];
 #pragma unroll
-    for (int v = 0; v < NV8; ++v) xv[v] = xn[v];
+  for (int v = 0; v < NV8; ++v) xa[v] = xp[32 * v];
+  for (int i = 0; i < nr; i += 2) {
+    if (i + 1 < nr) {
+#pragma unroll
+      for (int v = 0; v < NV8; ++v) xb[v] = xp[step + 32 * v];
+    }
+    row_out(xa, op);
+    if (i + 1 >= nr) break;
+    if (i + 2 < nr) {
+#pragma unroll
+      for (int v = 0; v < NV8; ++v) xa[v] = xp[2 * step + 32 * v];
+    }
+    row_out(xb, op + step);
+    xp += 2 * step;
+    op += 2 * step;
   }
 }
 
