@@ -11,6 +11,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -109,8 +110,9 @@ struct Launch {
   anvil_op op;
   // resolved device pointers, one per op.off slot
   void *ptr[8];
-  // GEMM tensor-core path
+  // GEMM tensor-core path; pair: 256-row tiles over CTA pairs (BN = 256)
   bool tc = false;
+  bool pair = false;
   int bn = 0;
   CUtensorMap mapA, mapB, mapC;
   GemmParams gp;
@@ -132,6 +134,7 @@ struct anvil_model {
   std::vector<cudaEvent_t> events;
   // pipelined enqueues: recorded after this model's last input copies and after its last launch chain
   cudaEvent_t ev_in = nullptr, ev_run = nullptr;
+  int pair_clusters = -1;            // co-resident CTA pairs of the pair GEMM (0: the pair path is off)
 };
 
 extern "C" int anvil_device_count(int *count) {
@@ -209,6 +212,11 @@ static int kernel_attrs(int device) {
   r |= set_smem(qgemm_tc_kernel<BN, OB, true>, TcCfg<BN>::SMEM_BYTES);
     TC_ATTR(64, 1) TC_ATTR(64, 2) TC_ATTR(128, 1) TC_ATTR(128, 2) TC_ATTR(256, 1) TC_ATTR(256, 2)
 #undef TC_ATTR
+#define TC_PAIR_ATTR(OB)                                                                   \
+  r |= set_smem(qgemm_tc_kernel<256, OB, false, true>, TcCfg<256, true>::SMEM_BYTES);    \
+  r |= set_smem(qgemm_tc_kernel<256, OB, true, true>, TcCfg<256, true>::SMEM_BYTES);
+    TC_PAIR_ATTR(1) TC_PAIR_ATTR(2)
+#undef TC_PAIR_ATTR
     if (r) return ANVIL_E_CUDA;
     attrs[device] = true;
   }
@@ -250,6 +258,42 @@ static int resolve(anvil_model *m, const anvil_op &op, int slot, uint64_t bytes,
 }
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Launch configuration of the pair GEMM: clusters of two CTAs (one per SM of a neighbouring pair).
+static cudaLaunchConfig_t pair_config(dim3 grid, cudaStream_t st, cudaLaunchAttribute *attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = TcCfg<256, true>::SMEM_BYTES;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// How many CTA pairs of the pair GEMM fit on the device at once (0 turns the pair path off; so does
+// ANVIL_GEMM_PAIR=0 in the environment).
+static int pair_clusters(anvil_model *m) {
+  if (m->pair_clusters < 0) {
+    const char *env = getenv("ANVIL_GEMM_PAIR");
+    int n = 0;
+    if (!env || atoi(env) != 0) {
+      cudaLaunchAttribute attr[1];
+      cudaLaunchConfig_t cfg = pair_config(dim3((unsigned)(m->sms & ~1)), m->stream, attr);
+      if (cudaOccupancyMaxActiveClusters(&n, qgemm_tc_kernel<256, 1, false, true>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+      }
+    }
+    m->pair_clusters = n;
+  }
+  return m->pair_clusters;
+}
+
 
 // tc GEMMs with i8 row-major outputs of 256-column tiles store through TMA (32 rows x 64 bytes per epilogue warp);
 // the tensor map goes in L.mapC and sets gp.tma_store. Other outputs keep the per-lane global stores.
@@ -349,13 +393,18 @@ static int prepare_gemm(anvil_model *m, Launch &L) {
   L.tc = tc_ok;
   if (!tc_ok) return ANVIL_OK;
   L.bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
-  p.m_tiles = (M + TC_BM - 1) / TC_BM;
+  // wide outputs over many rows: 256-row tiles on CTA pairs, each SM staging half of every B tile, which relieves
+  // the shared-memory traffic of the main loop. A fused residual epilogue over a short K is bound by its own
+  // residual reads and keeps single-CTA tiles (measured: 768 x 768 residual GEMM 58 us single, 60 us paired).
+  L.pair = L.bn == 256 && M >= 4 * TC_BM && !(p.res && K < 2048) && pair_clusters(m) > 0;
+  const int64_t tile_rows = L.pair ? 2 * TC_BM : TC_BM;
+  p.m_tiles = (M + tile_rows - 1) / tile_rows;
   p.n_tiles = (N + L.bn - 1) / L.bn;
   p.tiles = batch * p.m_tiles * p.n_tiles;
   const uint64_t a_z = batch, a_zs = a_bs ? a_bs : M * K;
   const uint64_t b_z = bt_bs ? batch : 1, b_zs = bt_bs ? bt_bs : N * K;
   if ((rc = make_map_i8(&L.mapA, p.A, K, M, a_z, K, a_zs, TC_BM))) return rc;
-  if ((rc = make_map_i8(&L.mapB, p.BT, K, N, b_z, K, b_zs, L.bn))) return rc;
+  if ((rc = make_map_i8(&L.mapB, p.BT, K, N, b_z, K, b_zs, L.pair ? L.bn / 2 : L.bn))) return rc;
   return gemm_out_map(L);
 }
 
@@ -524,7 +573,19 @@ static int launch_op(anvil_model *m, Launch &L) {
   switch (op.kind) {
     case ANVIL_OP_GEMM: {
       GemmParams &p = L.gp;
-      if (L.tc) {
+      if (L.tc && L.pair) {
+        const int ncl = (int)std::min<int64_t>(p.tiles, pair_clusters(m));
+        cudaLaunchAttribute attr[1];
+        const cudaLaunchConfig_t cfg = pair_config(dim3((unsigned)(2 * ncl)), st, attr);
+        cudaError_t e;
+        if (op.out_bytes == 1)
+          e = cudaLaunchKernelEx(&cfg, p.res ? qgemm_tc_kernel<256, 1, true, true> : qgemm_tc_kernel<256, 1, false, true>,
+                                 L.mapA, L.mapB, L.mapC, p);
+        else
+          e = cudaLaunchKernelEx(&cfg, p.res ? qgemm_tc_kernel<256, 2, true, true> : qgemm_tc_kernel<256, 2, false, true>,
+                                 L.mapA, L.mapB, L.mapC, p);
+        if (e != cudaSuccess) return fail(ANVIL_E_CUDA, "op %d: pair gemm launch failed: %s", oi, cudaGetErrorString(e));
+      } else if (L.tc) {
         const int grid = (int)std::min<int64_t>(p.tiles, m->sms);
 #define TC_LAUNCH(BN, OB)                                                                                       \
   do {                                                                                                          \

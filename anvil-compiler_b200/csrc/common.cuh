@@ -281,6 +281,80 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
                : "memory");
 }
 
+// ------------------------------------------------------------------------------------------- CTA pairs
+// A cluster of two CTAs on neighbouring SMs computes one 256-row MMA tile (tcgen05 cta_group::2): each CTA stages
+// its 128 rows of A and half of B's rows in its own shared memory, the even CTA (rank 0) issues the MMAs, and each
+// CTA's TMEM receives its own 128 accumulator rows.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The shared::cluster address of the variable at shared::cta address `addr` in the cluster's CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Every thread of both CTAs: prior shared-memory writes (barrier inits included) are visible cluster-wide after.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (this CTA's or the peer's), with the default
+// (CTA-scope release) semantics: a cluster-scope release would fence all of the thread's outstanding memory
+// operations first. The accumulator hand-off it signals is ordered by the tcgen05 fences around it.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// TMA tile load into this CTA's shared memory whose completion (bytes) is counted on an mbarrier that may sit in
+// the peer CTA (shared::cluster address), as the pair's loads all complete on the even CTA's barrier.
+__device__ __forceinline__ void tma_load_3d_pair(void *smem_dst, const CUtensorMap *map, int x, int y, int z,
+                                                 uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], "
+      "[%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+// TMEM allocation of both CTAs of the pair: one warp of each CTA (the same warp index, the same slot offset).
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *smem_slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D (+)= A * B over the pair, int8 x int8 -> int32: issued by the even CTA with descriptors of its own shared
+// memory; the peer's operand halves sit at the same offsets in the peer CTA.
+__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the barrier at this offset in both CTAs of the pair once the pair MMAs issued before have completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
 // 32 lanes x 32 consecutive columns of 32-bit TMEM cells: thread i of the warp gets lane (base lane + i).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, int32_t (&r)[16]) {
   asm volatile(

@@ -149,10 +149,12 @@ constexpr int TC_EPI_WARPS = 16;          // four warps per TMEM lane quarter, e
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;   // warp 0 TMA, warp 1 MMA, warps 2-17 epilogue
 constexpr int TC_SMEM_RING = 192 * 1024;  // bytes of A/B stages
 
-template <int BN>
+// PAIR: the CTA is one of a cluster pair sharing 256-row tiles (cta_group::2) and stages BN / 2 rows of B.
+template <int BN, bool PAIR = false>
 struct TcCfg {
   static constexpr int A_BYTES = TC_BM * TC_BK;
-  static constexpr int B_BYTES = BN * TC_BK;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+  static constexpr int B_BYTES = B_ROWS * TC_BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = TC_SMEM_RING / STAGE_BYTES > 8 ? 8 : TC_SMEM_RING / STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;     // two accumulators
@@ -284,11 +286,17 @@ __device__ __forceinline__ void store_row32(typename IntOf<OB>::T *dst, const in
   }
 }
 
-template <int BN, int OB, bool RES>
+// PAIR (launched as clusters of 2): tile t of the pair covers rows [256 mb, 256 mb + 256); CTA rank r loads and
+// drains rows 256 mb + 128 r .. + 128 and stages B rows nb*BN + r*BN/2 .. + BN/2. Both CTAs' loads complete on the
+// even CTA's full barrier (its producer expects both halves' bytes), the even CTA's MMA warp issues the 256-row
+// MMAs and commits to the empty / accumulator-full barriers of both CTAs, and every epilogue warp of either CTA
+// releases an accumulator on the even CTA's barrier. Every wait is bounded as in the single-CTA kernel.
+template <int BN, int OB, bool RES, bool PAIR = false>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using Cfg = TcCfg<BN>;
+  using Cfg = TcCfg<BN, PAIR>;
+  constexpr int TMR = PAIR ? 2 * TC_BM : TC_BM;       // rows of one tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align_smem_1024(smem_raw);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + Cfg::BAR_OFF);
@@ -302,6 +310,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   int32_t *bst = reinterpret_cast<int32_t *>(smem + Cfg::BST_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int64_t t_first = PAIR ? (blockIdx.x >> 1) : blockIdx.x, t_step = PAIR ? (gridDim.x >> 1) : gridDim.x;
   if (threadIdx.x == 0) {
     for (int i = 0; i < Cfg::STAGES; ++i) {
       mbar_init(&full[i], 1);
@@ -309,7 +319,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 32 * TC_EPI_WARPS);
+      // single CTA: every epilogue thread arrives; pair: one arrival per epilogue warp of both CTAs
+      mbar_init(&tempty[i], PAIR ? 2 * TC_EPI_WARPS : 32 * TC_EPI_WARPS);
     }
     *abort = 0;
     fence_mbar_init();
@@ -321,9 +332,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   if (p.lut)
     for (int i = threadIdx.x; i < 32 * 256; i += TC_THREADS) lut_r[i] = p.lut[i >> 5];
-  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (PAIR) tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    else tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) {                           // the peer's barriers are initialised before any remote use
+    __syncwarp();
+    cluster_sync();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int num_kb = (int)((p.K + TC_BK - 1) / TC_BK);
@@ -334,36 +352,58 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0, armed = 0, armed_phase = 0;     // per stage: armed at least once, parity of last arm
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+      for (int64_t t = t_first; t < p.tiles && ok; t += t_step) {
         const int64_t nb = t % p.n_tiles, rest = t / p.n_tiles;
         const int64_t mb = rest % p.m_tiles, bb = rest / p.m_tiles;
+        const int row0 = (int)(mb * TMR + rank * TC_BM);
+        const int bz = p.bt_bstride ? (int)bb : 0;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort, p.flags, p.op_index)) { ok = false; break; }
           armed |= 1u << stage;
           armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
           uint8_t *sa = smem + stage * Cfg::STAGE_BYTES;
           uint8_t *sb = sa + Cfg::A_BYTES;
-          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          tma_load_3d(sa, &tmA, kb * TC_BK, (int)(mb * TC_BM), (int)bb, &full[stage]);
-          tma_load_3d(sb, &tmB, kb * TC_BK, (int)(nb * BN), p.bt_bstride ? (int)bb : 0, &full[stage]);
+          if constexpr (PAIR) {
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::STAGE_BYTES);
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            tma_load_3d_pair(sa, &tmA, kb * TC_BK, row0, (int)bb, fb);
+            tma_load_3d_pair(sb, &tmB, kb * TC_BK, (int)(nb * BN + rank * Cfg::B_ROWS), bz, fb);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+            tma_load_3d(sa, &tmA, kb * TC_BK, row0, (int)bb, &full[stage]);
+            tma_load_3d(sb, &tmB, kb * TC_BK, (int)(nb * BN), bz, &full[stage]);
+          }
           if (++stage == nst) { stage = 0; phase ^= 1u; }
         }
       }
       if (!ok) {      // aborted: let every tile load already issued land before the CTA's smem is released
-        for (int s = 0; s < nst; ++s)
-          if (armed & (1u << s)) mbar_wait_ns(&full[s], (armed_phase >> s) & 1u, 10000000ull);
+        if constexpr (PAIR) {
+          // this CTA's loads complete on the even CTA's barrier: give them a fixed 2 ms to land
+          const uint64_t t0 = globaltimer();
+          while (globaltimer() - t0 < 2000000ull) {}
+        } else {
+          for (int s = 0; s < nst; ++s)
+            if (armed & (1u << s)) mbar_wait_ns(&full[s], (armed_phase >> s) & 1u, 10000000ull);
+        }
+      } else if (PAIR) {
+        // the MMA commits of the last fills arrive on this CTA's empty barriers: take every stage once more so
+        // that none is still in flight when the pair exits
+        for (int i = 0; i < nst; ++i) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort, p.flags, p.op_index)) break;
+          if (++stage == nst) { stage = 0; phase ^= 1u; }
+        }
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (elect_one()) {
-      constexpr uint32_t idesc = idesc_i8(TC_BM, BN);
+    // ------------------------------------------------------------------ MMA issuer (the even CTA of a pair)
+    if ((!PAIR || rank == 0) && elect_one()) {
+      constexpr uint32_t idesc = idesc_i8(TMR, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t aphase = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+      for (int64_t t = t_first; t < p.tiles && ok; t += t_step) {
         if (!mbar_wait(&tempty[acc], aphase ^ 1u, abort, p.flags, p.op_index)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -374,14 +414,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const uint32_t sb = sa + Cfg::A_BYTES;
 #pragma unroll
           for (int k = 0; k < TC_BK / 32; ++k) {
-            mma_i8(d_tmem, sw128_kmajor_desc(sa + 32 * k), sw128_kmajor_desc(sb + 32 * k), idesc,
-                   (kb > 0 || k > 0) ? 1u : 0u);
+            if constexpr (PAIR)
+              mma_i8_pair(d_tmem, sw128_kmajor_desc(sa + 32 * k), sw128_kmajor_desc(sb + 32 * k), idesc,
+                          (kb > 0 || k > 0) ? 1u : 0u);
+            else
+              mma_i8(d_tmem, sw128_kmajor_desc(sa + 32 * k), sw128_kmajor_desc(sb + 32 * k), idesc,
+                     (kb > 0 || k > 0) ? 1u : 0u);
           }
-          mma_commit(&empty[stage]);
+          if constexpr (PAIR) mma_commit_pair(&empty[stage]);
+          else mma_commit(&empty[stage]);
           if (++stage == nst) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        mma_commit(&tfull[acc]);
+        if constexpr (PAIR) mma_commit_pair(&tfull[acc]);
+        else mma_commit(&tfull[acc]);
         if (++acc == 2) { acc = 0; aphase ^= 1u; }
       }
     }
@@ -414,10 +460,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // the folded bias of a sub-chunk's 16 columns (lanes 0-15), loaded one sub-chunk ahead like the residual
     const bool bias_pre = p.bias && !p.check;
     bool bad = false;
-    for (int64_t t = blockIdx.x; t < p.tiles; t += gridDim.x) {
+    const uint32_t tempty0 = PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
+    for (int64_t t = t_first; t < p.tiles; t += t_step) {
       const int64_t nb = t % p.n_tiles, rest = t / p.n_tiles;
       const int64_t mb = rest % p.m_tiles, bb = rest / p.m_tiles;
-      const int64_t row = mb * TC_BM + lane_base + lane;
+      const int64_t row0 = mb * TMR + rank * TC_BM;
+      const int64_t row = row0 + lane_base + lane;
       const bool row_ok = row < p.M;
       const int64_t cbase = nb * BN + cq * Cfg::COLS;
       uint4 rcur = make_uint4(0, 0, 0, 0), rnxt = make_uint4(0, 0, 0, 0);
@@ -540,13 +588,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         bcur = bnxt;
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      if constexpr (PAIR) {                            // every lane's TMEM loads have completed (wait::ld)
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty0 + 8u * (uint32_t)acc);
+      } else {
+        mbar_arrive(&tempty[acc]);
+      }
       if (++acc == 2) { acc = 0; aphase ^= 1u; }
       if (tma_st) {
         fence_proxy_async();
         __syncwarp();
-        if (lane == 0) {
-          const int64_t r0 = mb * TC_BM + lane_base;
+        if (lane == 0 && row0 + lane_base < p.M) {    // a pair's odd CTA may have no rows left in the last tile
+          const int64_t r0 = row0 + lane_base;
           const int c0 = (int)cbase;
           if (tmode == 2) tma_store_3d(&tmC, stg_w, (int)(r0 % p.o_group), c0, (int)(r0 / p.o_group));
           else if (p.batch > 1) tma_store_3d(&tmC, stg_w, c0, (int)r0, (int)bb);
@@ -560,9 +613,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) {                           // neither CTA's shared memory or barriers are used any more
+    __syncwarp();
+    cluster_sync();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 

@@ -65,6 +65,51 @@ def test_gemm_requant_bit_exact(m, n, k, path):
     assert np.array_equal(out.cpu().numpy().astype(np.int64), want)
 
 
+def _pair_gemm_case(seed, T, K, N, kind):
+    """x [T, K] -> qlinear to N columns (with a bias, a LUT epilogue or an i16 result) [-> residual add of r]."""
+    from anvil.frontend.numerics import fixed_point
+    from anvil.ir.graph import GraphBuilder
+    rng = np.random.default_rng(seed)
+    g = GraphBuilder("pair")
+    consts = {}
+
+    def const(name, shape, dtype="i8", value=None):
+        consts[name] = np.asarray(value, dtype=np.int64)
+        return g.const(name, list(shape), dtype)
+
+    wv = rng.integers(-127, 128, (K, N))
+    (m,), s = fixed_point([40.0 / (50.0 * 73 * np.sqrt(K)) * rng.uniform(0.7, 1.4)],
+                          [128 * int(np.abs(wv).sum(axis=0).max()) + 3000])
+    x = g.input("x", [T, K])
+    r = g.input("r", [T, N]) if kind == "residual" else None     # declared first: the fused epilogue reads it
+    bias = const("b", [N], "i32", rng.integers(-3000, 3001, N)) if kind in ("bias", "residual") else None
+    lut = const("lut", [256], value=rng.integers(-128, 128, 256)) if kind == "lut" else None
+    y = g.qlinear("y", x, const("w", [K, N], value=wv), m, s, lut=lut, dtype="i16" if kind == "i16" else "i8",
+                  bias=bias)
+    inputs = {"x": rng.integers(-128, 128, (T, K))}
+    if kind == "residual":
+        y = g.add_requant("out", r, y, 3, 5, 3)
+        inputs["r"] = rng.integers(-128, 128, (T, N))
+    g.output(y)
+    return g.module(), consts, inputs
+
+
+@pytest.mark.parametrize("T,K,N,kind", [(612, 128, 256, "bias"), (700, 768, 768, "lut"), (520, 256, 300, "residual"),
+                                        (1024, 64, 512, "i16"), (2048, 768, 768, "bias"), (1536, 3072, 768, "residual")])
+@pytest.mark.parametrize("pair", [True, False])
+@pytest.mark.parametrize("checked", [False, True])
+def test_pair_gemm_tiles_bit_exact(T, K, N, kind, pair, checked, monkeypatch):
+    """GEMMs wide enough for 256-column tiles over hundreds of rows run as 256-row tiles on CTA pairs
+    (ANVIL_GEMM_PAIR=0 keeps 128-row tiles on single CTAs): ragged last row and column tiles, a pair whose odd CTA
+    has no rows left, bias / LUT / i16 / fused-residual epilogues, checked and unchecked, vs the oracle."""
+    monkeypatch.setenv("ANVIL_GEMM_PAIR", "1" if pair else "0")
+    module, consts, inputs = _pair_gemm_case(T * 3 + K + N, T, K, N, kind)
+    want = interp.run(module, inputs, consts)
+    cm = anvil.compile(module, consts=consts, params=CudaParams(checked=checked, gemm="tc"))
+    res = cm.run([inputs[s] for s in cm.inputs], "cuda", quantized=True)
+    _check(res.ints, want.values, cm.outputs)
+
+
 # --------------------------------------------------------------------------------------------- whole graphs
 
 @pytest.mark.parametrize("seed", range(24))
