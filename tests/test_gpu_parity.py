@@ -324,11 +324,10 @@ def test_fused_attention_bit_exact(T, C, nh, causal, T2):
     _check(unfused.run([xb[s] for s in cm.inputs], "cuda", quantized=True).ints, want.values, cm.outputs)
 
 
-def _norm_case(seed, d, kind, with_bias, c):
+def _norm_case(seed, d, kind, with_bias, c, T=300):
     from anvil.ir.graph import GraphBuilder
     from graphs import mult_shift, rsqrt_lut
     rng = np.random.default_rng(seed)
-    T = 300
     g = GraphBuilder("norm")
     consts = {"w": rng.integers(-128, 128, d), "rs": rsqrt_lut(1024)}
     x = g.input("x", [T, d], "i8")
@@ -364,6 +363,16 @@ def test_norm_rows_bit_exact(d, kind, with_bias, c, checked):
     module, consts, xs = _norm_case(d * 7 + c, d, kind, with_bias, c)
     want = interp.run(module, {"x": xs}, consts, batch=True)
     cm = anvil.compile(module, consts=consts, prove=False, params=CudaParams(checked=checked))
+    _check(cm.run(xs, "cuda", quantized=True).ints, want.values, cm.outputs)
+
+
+@pytest.mark.parametrize("d", [256, 768, 2048])
+def test_norm_rows_many_per_warp(d):
+    """2 x 9000 LayerNorm rows (unchecked, the register-resident row kernel): more rows than resident warps, so every
+    warp walks several rows through its ring of row buffers, with ragged per-warp row counts."""
+    module, consts, xs = _norm_case(d * 11, d, "layernorm", True, 0, T=9000)
+    want = interp.run(module, {"x": xs}, consts, batch=True)
+    cm = anvil.compile(module, consts=consts, prove=False, params=CudaParams(checked=False))
     _check(cm.run(xs, "cuda", quantized=True).ints, want.values, cm.outputs)
 
 
