@@ -332,6 +332,9 @@ def run_ours(args):
     roofline = {k: v for k, v in roofs[dominant].items() if k != "total_us"}
     roofline["traffic"] = _traffic_from_profiles(dominant)
     gemm_roof = {k: v for k, v in roofs["gemm"].items() if k != "total_us"} if "gemm" in roofs else None
+    norm_roof = {k: v for k, v in roofs["norm"].items() if k != "total_us"} if "norm" in roofs else None
+    if norm_roof is not None:
+        norm_roof["traffic"] = _traffic_from_profiles("norm")
     # e2e through the public API: quantized input from pinned memory, the output read back into pinned memory
     outs = {}
     for s in cm.outputs:
@@ -359,6 +362,7 @@ def run_ours(args):
                     "d2h_bytes_per_step": int(out_bytes)},
             "roofline": roofline,
             "roofline_int8_gemm": gemm_roof,
+            "roofline_norm": norm_roof,
             "kernel_us_by_kind": dict(sorted(by_kind.items(), key=lambda kv: -kv[1])),
             "launch_us": [[d.label, C.KIND_NAMES[d.kind], round(u, 2)] for d, u in zip(prog.devops, kus)],
             "gpu_launches": sum(1 for d in prog.devops if d.kind != C.OP_COPY) * args.steps,
@@ -373,6 +377,17 @@ def run_ours(args):
     if dist is not None:
         dist.destroy_process_group()
     return 0
+
+
+# What each family's ncu capture shows it waits on (the summaries under profiles/ give the figures).
+LIMITERS = {
+    "attention": "integer issue of the 16 softmax warps (about 23 instructions per kept score element across the "
+                 "requant / row-sum / probability passes; ALU pipe the busiest), not the tensor pipe or DRAM: "
+                 "profiles/attn_kernel_c3_b64.md",
+    "gemm": "K = 3072: the tensor pipe (88 % active); K = 768: the epilogue warps draining each accumulator "
+            "(requant, bias, LUT or residual, pack, TMA store): profiles/qgemm_tc_c3_b64.md",
+    "norm": "instruction issue and row-load latency of one warp per 768-byte row: profiles/norm_row_c3_b64.md",
+}
 
 
 def _rooflines(prog, kus, hbm, bf16, src, C, i8peak=None):
@@ -409,6 +424,8 @@ def _rooflines(prog, kus, hbm, bf16, src, C, i8peak=None):
         out[k] = {"kernel": k, "bound": bound, "achieved": ach, "peak": peak, "unit": unit, "frac": ach / peak,
                   **extra, "peak_source": ps, "avg_launch_us": avg, "launches_per_step": f["n"],
                   "total_us": f["us"], **per}
+        if k in LIMITERS:
+            out[k]["limiter"] = LIMITERS[k]
     return out
 
 
@@ -461,7 +478,7 @@ def _traffic_from_profiles(kind):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c5"])
     ap.add_argument("--batch", type=int, default=0)
