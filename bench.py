@@ -217,6 +217,9 @@ def cpu_baseline(cfg, cm, gen, seqs=CPU_SAMPLE_SEQS):
                       f"float64 BLAS), {dt:.2f} s"}
 
 
+REFERENCE_BUDGET_S = 240.0
+
+
 def run_reference(args):
     """The CPU oracle (the numpy restatement of anvil.interp) on the host cores: a spawn pool, one sequence of the
     config per worker per step."""
@@ -235,6 +238,9 @@ def run_reference(args):
     payload = (print_ir(cm.module), cm.consts, in_sym, cm.meta[in_sym][1], cm.meta[in_sym][0], cm.meta[in_sym][2])
     ctx = mp.get_context("spawn")
     times = []
+    # a step is one whole sequence per worker (several seconds of single-threaded numpy); the timed steps stop
+    # early, with the count reported, once REFERENCE_BUDGET_S has passed, so any --steps ends within minutes
+    t_start = None
     with ctx.Pool(cores, initializer=_pool_init, initargs=(payload,)) as pool:
         for step in range(args.warmup + args.steps):
             t = time.perf_counter()
@@ -242,9 +248,13 @@ def run_reference(args):
             dt = time.perf_counter() - t
             if step >= args.warmup:
                 times.append(dt)
+                t_start = t_start if t_start is not None else t
+                if time.perf_counter() - t_start > REFERENCE_BUDGET_S:
+                    break
     tok = cores * seq
     value = tok * len(times) / sum(times)
-    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": len(times),
+            "steps_requested": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8/int32", "data": "synthetic",
             "impl": "reference",
@@ -478,7 +488,8 @@ def _traffic_from_profiles(kind):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: 200 for this arm, 3 for --impl reference)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c3", choices=["c1", "c2", "c3", "c5"])
     ap.add_argument("--batch", type=int, default=0)
@@ -493,7 +504,11 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
+        if args.steps is None:
+            args.steps = 3
         return run_reference(args)
+    if args.steps is None:
+        args.steps = 200
     return run_ours(args)
 
 
