@@ -328,6 +328,26 @@ static int gemm_out_map(Launch &L) {
   return ANVIL_OK;
 }
 
+// The tile decode's divisors: (m, s) of tile_div (gemm.cuh) for d = n_tiles and m_tiles; tiles must stay < 2^31.
+static int tile_magics(GemmParams &p, int op_index) {
+  if (p.tiles >= (1ll << 31)) return fail(ANVIL_E_BAD_ARG, "op %d: %lld gemm tiles (at most 2^31 - 1)", op_index,
+                                          (long long)p.tiles);
+  auto magic = [](int64_t d, uint32_t *m, int *s) {
+    if (d <= 1) {
+      *m = 0;
+      *s = 0;
+      return;
+    }
+    int l = 0;
+    while ((1ll << l) < d) ++l;                   // ceil(log2 d)
+    *m = (uint32_t)(((1ull << (31 + l)) + (uint64_t)d - 1) / (uint64_t)d);
+    *s = l - 1;
+  };
+  magic(p.n_tiles, &p.n_magic, &p.n_shift);
+  magic(p.m_tiles, &p.m_magic, &p.m_shift);
+  return ANVIL_OK;
+}
+
 static int prepare_gemm(anvil_model *m, Launch &L) {
   const anvil_op &op = L.op;
   const int64_t batch = op.dims[0], M = op.dims[1], N = op.dims[2], K = op.dims[3];
@@ -401,6 +421,7 @@ static int prepare_gemm(anvil_model *m, Launch &L) {
   p.m_tiles = (M + tile_rows - 1) / tile_rows;
   p.n_tiles = (N + L.bn - 1) / L.bn;
   p.tiles = batch * p.m_tiles * p.n_tiles;
+  if ((rc = tile_magics(p, op.op_index))) return rc;
   const uint64_t a_z = batch, a_zs = a_bs ? a_bs : M * K;
   const uint64_t b_z = bt_bs ? batch : 1, b_zs = bt_bs ? bt_bs : N * K;
   if ((rc = make_map_i8(&L.mapA, p.A, K, M, a_z, K, a_zs, TC_BM))) return rc;
@@ -994,6 +1015,7 @@ extern "C" int anvil_gemm_requant(const int8_t *A, const int8_t *BT, int8_t *out
     p.m_tiles = (M + TC_BM - 1) / TC_BM;
     p.n_tiles = (N + L.bn - 1) / L.bn;
     p.tiles = p.m_tiles * p.n_tiles;
+    if (int trc = tile_magics(p, -1)) return trc;
     int rc;
     if ((rc = make_map_i8(&L.mapA, A, K, M, 1, K, M * K, TC_BM))) return rc;
     if ((rc = make_map_i8(&L.mapB, BT, K, N, 1, K, N * K, L.bn))) return rc;
@@ -1082,6 +1104,7 @@ extern "C" int anvil_gemm_requant_noalloc(const int8_t *A, const int8_t *BT, int
     p.m_tiles = (M + TC_BM - 1) / TC_BM;
     p.n_tiles = (N + L.bn - 1) / L.bn;
     p.tiles = p.m_tiles * p.n_tiles;
+    if (int trc = tile_magics(p, -1)) return trc;
     int rc;
     if ((rc = make_map_i8(&L.mapA, A, K, M, 1, K, M * K, TC_BM))) return rc;
     if ((rc = make_map_i8(&L.mapB, BT, K, N, 1, K, N * K, L.bn))) return rc;

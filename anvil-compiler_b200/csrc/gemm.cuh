@@ -33,7 +33,9 @@ struct GemmParams {
   int check;
   uint32_t *flags;
   int op_index;
-  int64_t m_tiles, n_tiles, tiles;     // tc path tiling
+  int64_t m_tiles, n_tiles, tiles;     // tc path tiling (tiles < 2^31)
+  uint32_t n_magic, m_magic;           // tile_div: x / n_tiles and x / m_tiles for x < 2^31
+  int n_shift, m_shift;
   // fused residual add (unchecked only): out = clamp((res*ma + y*mb + 2^(s2-1)) >> s2) where y is the requant
   // result clamped to y_bytes' range and res is (M, N) row-major with res_bytes per element
   const void *res;
@@ -43,6 +45,13 @@ struct GemmParams {
   // head-major transposed layout (element (r, c) at (r / o_group) * o_gstride + c * o_group + r % o_group)
   int tma_store;
 };
+
+// x / d for 0 <= x < 2^31 and d >= 1, from the host's tile_magics (m, s): with l = ceil(log2 d) and
+// m = ceil(2^(31 + l) / d) (< 2^32), floor(x m / 2^(31 + l)) = floor(x / d) for every x < 2^31 (Granlund &
+// Montgomery, "Division by invariant integers using multiplication", 1994); s = l - 1. d = 1 is taken apart.
+__device__ __forceinline__ uint32_t tile_div(uint32_t x, uint32_t d, uint32_t m, int s) {
+  return d == 1 ? x : (__umulhi(x, m) >> s);
+}
 
 // y -> the fused residual add's result (32-bit exact under the static int32 proof)
 template <int OB>
@@ -312,6 +321,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   const int64_t t_first = PAIR ? (blockIdx.x >> 1) : blockIdx.x, t_step = PAIR ? (gridDim.x >> 1) : gridDim.x;
+  const uint32_t nt = (uint32_t)p.n_tiles, mt = (uint32_t)p.m_tiles;
   if (threadIdx.x == 0) {
     for (int i = 0; i < Cfg::STAGES; ++i) {
       mbar_init(&full[i], 1);
@@ -353,8 +363,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint32_t phase = 0, armed = 0, armed_phase = 0;     // per stage: armed at least once, parity of last arm
       bool ok = true;
       for (int64_t t = t_first; t < p.tiles && ok; t += t_step) {
-        const int64_t nb = t % p.n_tiles, rest = t / p.n_tiles;
-        const int64_t mb = rest % p.m_tiles, bb = rest / p.m_tiles;
+        const uint32_t rest = tile_div((uint32_t)t, nt, p.n_magic, p.n_shift), nb = (uint32_t)t - rest * nt;
+        const uint32_t bb = tile_div(rest, mt, p.m_magic, p.m_shift), mb = rest - bb * mt;
         const int row0 = (int)(mb * TMR + rank * TC_BM);
         const int bz = p.bt_bstride ? (int)bb : 0;
         for (int kb = 0; kb < num_kb; ++kb) {
@@ -462,9 +472,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     bool bad = false;
     const uint32_t tempty0 = PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
     for (int64_t t = t_first; t < p.tiles; t += t_step) {
-      const int64_t nb = t % p.n_tiles, rest = t / p.n_tiles;
-      const int64_t mb = rest % p.m_tiles, bb = rest / p.m_tiles;
-      const int64_t row0 = mb * TMR + rank * TC_BM;
+      const uint32_t rest = tile_div((uint32_t)t, nt, p.n_magic, p.n_shift), nb = (uint32_t)t - rest * nt;
+      const uint32_t bb = tile_div(rest, mt, p.m_magic, p.m_shift), mb = rest - bb * mt;
+      const int64_t row0 = (int64_t)mb * TMR + rank * TC_BM;
       const int64_t row = row0 + lane_base + lane;
       const bool row_ok = row < p.M;
       const int64_t cbase = nb * BN + cq * Cfg::COLS;
@@ -489,8 +499,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __syncwarp();
       }
       using TO = typename IntOf<OB>::T;
-      const int64_t R = p.o_group ? p.o_group : p.M;
-      TO *orow = reinterpret_cast<TO *>(p.out) + bb * p.o_bstride + (row / R) * p.o_gstride + (row % R) * p.o_rstride;
+      TO *orow = nullptr;                              // direct stores only (the TMA store path needs no row pointer)
+      if (!tma_st) {
+        const int64_t R = p.o_group ? p.o_group : p.M;
+        orow = reinterpret_cast<TO *>(p.out) + (int64_t)bb * p.o_bstride + (row / R) * p.o_gstride +
+               (row % R) * p.o_rstride;
+      }
 #pragma unroll 1
       for (int sc = 0; sc < NSC; ++sc) {
         const int c0 = cq * Cfg::COLS + sc * 16;
