@@ -328,23 +328,25 @@ static int gemm_out_map(Launch &L) {
   return ANVIL_OK;
 }
 
-// The tile decode's divisors: (m, s) of tile_div (gemm.cuh) for d = n_tiles and m_tiles; tiles must stay < 2^31.
+// (m, s) of tile_div (common.cuh) for the divisor d >= 1: m = ceil(2^(31 + l) / d), s = l - 1, l = ceil(log2 d).
+static void div_magic(int64_t d, uint32_t *m, int *s) {
+  if (d <= 1) {
+    *m = 0;
+    *s = 0;
+    return;
+  }
+  int l = 0;
+  while ((1ll << l) < d) ++l;
+  *m = (uint32_t)(((1ull << (31 + l)) + (uint64_t)d - 1) / (uint64_t)d);
+  *s = l - 1;
+}
+
+// The tile decode's divisors n_tiles and m_tiles; tiles must stay < 2^31.
 static int tile_magics(GemmParams &p, int op_index) {
   if (p.tiles >= (1ll << 31)) return fail(ANVIL_E_BAD_ARG, "op %d: %lld gemm tiles (at most 2^31 - 1)", op_index,
                                           (long long)p.tiles);
-  auto magic = [](int64_t d, uint32_t *m, int *s) {
-    if (d <= 1) {
-      *m = 0;
-      *s = 0;
-      return;
-    }
-    int l = 0;
-    while ((1ll << l) < d) ++l;                   // ceil(log2 d)
-    *m = (uint32_t)(((1ull << (31 + l)) + (uint64_t)d - 1) / (uint64_t)d);
-    *s = l - 1;
-  };
-  magic(p.n_tiles, &p.n_magic, &p.n_shift);
-  magic(p.m_tiles, &p.m_magic, &p.m_shift);
+  div_magic(p.n_tiles, &p.n_magic, &p.n_shift);
+  div_magic(p.m_tiles, &p.m_magic, &p.m_shift);
   return ANVIL_OK;
 }
 
@@ -478,6 +480,8 @@ static int prepare_attention(anvil_model *m, Launch &L) {
   a.causal = (op.flags & ANVIL_F_CAUSAL) ? 1 : 0;
   a.flags = m->flags;
   a.op_index = op.op_index;
+  div_magic((int64_t)B * H, &a.bh_magic, &a.bh_shift);
+  div_magic(H, &a.h_magic, &a.h_shift);
   L.hd = (int)HD;
   return ANVIL_OK;
 }

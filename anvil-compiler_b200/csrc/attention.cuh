@@ -37,6 +37,8 @@ struct AttnParams {
   int s1, s2, one, causal;
   uint32_t *flags;
   int op_index;
+  uint32_t bh_magic, h_magic;          // tile_div by B*H and by H (work-item decode)
+  int bh_shift, h_shift;
 };
 
 template <int HD>
@@ -106,12 +108,13 @@ struct AttnTile {
 };
 
 __device__ __forceinline__ AttnTile attn_tile(const AttnParams &p, int t) {
-  const int BH = p.B * p.H;
+  const uint32_t BH = (uint32_t)(p.B * p.H);
   AttnTile w;
-  const int qt = p.nqt - 1 - t / BH;
-  w.bh = t % BH;
-  w.b = w.bh / p.H;
-  w.h = w.bh % p.H;
+  const uint32_t r = tile_div((uint32_t)t, BH, p.bh_magic, p.bh_shift);
+  const int qt = p.nqt - 1 - (int)r;
+  w.bh = (int)((uint32_t)t - r * BH);
+  w.b = (int)tile_div((uint32_t)w.bh, (uint32_t)p.H, p.h_magic, p.h_shift);
+  w.h = w.bh - w.b * p.H;
   w.q0 = qt * 128;
   const int kv_end = p.causal ? min(p.T2, w.q0 + 128) : p.T2;
   w.nkv = (kv_end + 127) / 128;

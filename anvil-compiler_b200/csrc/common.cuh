@@ -97,6 +97,13 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// x / d for 0 <= x < 2^31 and d >= 1, from the host's div_magic(d) = (m, s): with l = ceil(log2 d) and
+// m = ceil(2^(31 + l) / d) (< 2^32), floor(x m / 2^(31 + l)) = floor(x / d) for every x < 2^31 (Granlund &
+// Montgomery, "Division by invariant integers using multiplication", 1994); s = l - 1. d = 1 is taken apart.
+__device__ __forceinline__ uint32_t tile_div(uint32_t x, uint32_t d, uint32_t m, int s) {
+  return d == 1 ? x : (__umulhi(x, m) >> s);
+}
+
 // ------------------------------------------------------------------------------------------------- mbarrier
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {

@@ -46,13 +46,6 @@ struct GemmParams {
   int tma_store;
 };
 
-// x / d for 0 <= x < 2^31 and d >= 1, from the host's tile_magics (m, s): with l = ceil(log2 d) and
-// m = ceil(2^(31 + l) / d) (< 2^32), floor(x m / 2^(31 + l)) = floor(x / d) for every x < 2^31 (Granlund &
-// Montgomery, "Division by invariant integers using multiplication", 1994); s = l - 1. d = 1 is taken apart.
-__device__ __forceinline__ uint32_t tile_div(uint32_t x, uint32_t d, uint32_t m, int s) {
-  return d == 1 ? x : (__umulhi(x, m) >> s);
-}
-
 // y -> the fused residual add's result (32-bit exact under the static int32 proof)
 template <int OB>
 __device__ __forceinline__ int residual_add(int y, int rv, const GemmParams &p) {
