@@ -721,12 +721,15 @@ static int launch_op(anvil_model *m, Launch &L) {
     case ANVIL_OP_TRANSPOSE: {
       TransposeDims td;
       td.rank = (int)d[0];
-      int64_t total = 1;
+      int64_t total = 1, span = 0;
       for (int i = 0; i < 6; ++i) {
         td.n[i] = i < td.rank ? d[1 + i] : 1;
         td.st[i] = i < td.rank ? op.strides[i] : 0;
         total *= td.n[i];
+        span += (td.n[i] - 1) * td.st[i];
+        div_magic(td.n[i], &td.mg[i], &td.sh[i]);
       }
+      td.small = total < (1ll << 31) && span < (1ll << 31);
       const int g = grid_for(m, total, 256);
       if (op.in_bytes == 1) transpose_kernel<1><<<g, 256, 0, st>>>(L.ptr[0], L.ptr[1], td, total);
       else if (op.in_bytes == 2) transpose_kernel<2><<<g, 256, 0, st>>>(L.ptr[0], L.ptr[1], td, total);

@@ -401,9 +401,11 @@ __global__ void softmax_kernel(const int8_t *__restrict__ x, const int32_t *__re
   const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   bool bad = false;
-  for (int64_t row = warp; row < rows; row += nwarps) {
-    const int i = (int)(row % t1);
-    const int kept = causal ? (i + 1 < t2 ? i + 1 : t2) : t2;
+  // row % t1, carried from row to row (the rows of a warp step by nwarps) instead of a division per row
+  const int64_t step_i = nwarps % t1;
+  int64_t i = warp % t1;
+  for (int64_t row = warp; row < rows; row += nwarps, i = i + step_i >= t1 ? i + step_i - t1 : i + step_i) {
+    const int kept = causal ? (int)(i + 1 < t2 ? i + 1 : t2) : t2;
     const int8_t *xr = x + row * t2;
     TO *orow = o + row * t2;
     int mx = -128;
@@ -437,6 +439,9 @@ struct TransposeDims {
   int64_t n[6];
   int64_t st[6];
   int rank;
+  int small;                           // total and source span < 2^31: 32-bit index decode by tile_div
+  uint32_t mg[6];                      // tile_div magics of n[]
+  int sh[6];
 };
 
 template <int EB>
@@ -444,6 +449,22 @@ __global__ void transpose_kernel(const void *__restrict__ x_, void *__restrict__
   using T = typename IntOf<EB>::T;
   const T *x = reinterpret_cast<const T *>(x_);
   T *o = reinterpret_cast<T *>(o_);
+  if (td.small) {
+    // dims past the rank have n = 1 and stride 0: their digit is 0 and they leave the quotient unchanged
+    const uint32_t stride = gridDim.x * blockDim.x, tot = (uint32_t)total;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < tot; i += stride) {
+      uint32_t rem = i, src = 0;
+#pragma unroll
+      for (int dd = 5; dd >= 0; --dd) {
+        const uint32_t nd = (uint32_t)td.n[dd];
+        const uint32_t q = tile_div(rem, nd, td.mg[dd], td.sh[dd]);
+        src += (rem - q * nd) * (uint32_t)td.st[dd];
+        rem = q;
+      }
+      o[i] = x[src];
+    }
+    return;
+  }
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
     int64_t rem = i, src = 0;
@@ -467,9 +488,11 @@ __global__ void embed_kernel(const int32_t *__restrict__ ids, const int8_t *__re
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const long long rnd = round_term(s);
   bool bad = false, badidx = false;
-  for (int64_t row = warp; row < rows; row += nwarps) {
+  // row % t carried from row to row (the rows of a warp step by nwarps) instead of a division per row
+  const int64_t step_pos = nwarps % t;
+  int64_t pos = warp % t;
+  for (int64_t row = warp; row < rows; row += nwarps, pos = pos + step_pos >= t ? pos + step_pos - t : pos + step_pos) {
     const int64_t id = ids[row];
-    const int pos = (int)(row % t);
     int8_t *orow = out + row * d;
     if (id < 0 || id >= vocab) {
       badidx = true;
