@@ -111,10 +111,14 @@ __global__ void __launch_bounds__(256) qgemm_simt_kernel(GemmParams p) {
   if (p.out_bytes == 1) { lo = -128; hi = 127; } else { lo = -32768; hi = 32767; }
   bool bad = false;
   const int8_t *lt = p.lut ? lut_s : nullptr;
+  const int64_t R = p.o_group ? p.o_group : p.M;
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     int64_t gi = i0 + ty + 16 * q;
     if (gi >= p.M) continue;
+    // the output row's offset, once per row (a 32-bit division when row and group fit)
+    const int64_t gq = (gi < (1ll << 31) && R < (1ll << 31)) ? (int64_t)((uint32_t)gi / (uint32_t)R) : gi / R;
+    const int64_t orow = b * p.o_bstride + gq * p.o_gstride + (gi - gq * R) * p.o_rstride;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       int64_t gj = j0 + tx + 16 * r;
@@ -134,8 +138,7 @@ __global__ void __launch_bounds__(256) qgemm_simt_kernel(GemmParams p) {
         const int rnd2 = p.shift2 ? 1 << (p.shift2 - 1) : 0;
         v = min(hi, max(lo, (rv * p.ma + v * p.mb + rnd2) >> p.shift2));
       }
-      const int64_t R = p.o_group ? p.o_group : p.M;
-      int64_t o = b * p.o_bstride + (gi / R) * p.o_gstride + (gi % R) * p.o_rstride + gj * p.o_cstride;
+      const int64_t o = orow + gj * p.o_cstride;
       if (p.out_bytes == 1) reinterpret_cast<int8_t *>(p.out)[o] = (int8_t)v;
       else reinterpret_cast<int16_t *>(p.out)[o] = (int16_t)v;
     }
