@@ -214,10 +214,9 @@ __global__ void __launch_bounds__(256) norm_vec_kernel(const int8_t *__restrict_
 #pragma unroll
         for (int q = 0; q < 16; ++q) sum += sext8(ws[q >> 2], q & 3);
       }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      const int num = sum + d / 2;                        // floor division by d > 0
-      mean = num >= 0 ? num / d : -((-num + d - 1) / d);
+      sum = __reduce_add_sync(0xffffffffu, sum);
+      // floor((sum + d/2) / d): |sum| <= 128 d, so the offset of 128 d makes the dividend positive
+      mean = (int)((unsigned)(sum + d / 2 + 128 * d) / (unsigned)d) - 128;
     }
     int ss = 0;
 #pragma unroll
@@ -230,12 +229,15 @@ __global__ void __launch_bounds__(256) norm_vec_kernel(const int8_t *__restrict_
         ss += (xc * xc + rc) >> c;
       }
     }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    ss = __reduce_add_sync(0xffffffffu, ss);
     ss += e;
-    int idx = ss, k = 0;
-    while (idx >= n) { idx >>= 2; ++k; }
-    const int r = lut[idx];
+    int k = 0;
+    if (ss >= n) {
+      // the smallest k with (ss >> 2k) < n: bit lengths give it to within one step
+      const int ka = max(0, (32 - __clz(ss) - (32 - __clz(n)) + 1) >> 1);
+      k = ka + ((ss >> (2 * ka)) >= n);
+    }
+    const int r = lut[ss >> (2 * k)];
     const int sh = s + k;
     const int rnd = sh ? 1 << (sh - 1) : 0;
     uint4 *orow = reinterpret_cast<uint4 *>(out + row * d);

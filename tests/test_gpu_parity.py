@@ -353,13 +353,13 @@ def _norm_case(seed, d, kind, with_bias, c, T=300):
     return g.module(), {k: np.asarray(v, dtype=np.int64) for k, v in consts.items()}, xs
 
 
-@pytest.mark.parametrize("d", [256, 768, 2048])
+@pytest.mark.parametrize("d", [64, 256, 400, 768, 2048])
 @pytest.mark.parametrize("kind,with_bias,c", [("layernorm", True, 0), ("layernorm", False, 0), ("rmsnorm", False, 0),
                                               ("layernorm", True, 3), ("rmsnorm", False, 2)])
 @pytest.mark.parametrize("checked", [False, True])
 def test_norm_rows_bit_exact(d, kind, with_bias, c, checked):
-    """LayerNorm / RMSNorm rows of i8 (the register-resident row kernel for d a multiple of 256 when unchecked, the
-    general row kernel when checked) vs the oracle, 2 x 300 rows with a per-row offset, saturated rows included."""
+    """LayerNorm / RMSNorm rows of i8 (unchecked: the register-resident row kernel for d a multiple of 256, the
+    16-byte-vector row kernel for other multiples of 16; checked: the general row kernel) vs the oracle, 2 x 300 rows with a per-row offset, saturated rows included."""
     module, consts, xs = _norm_case(d * 7 + c, d, kind, with_bias, c)
     want = interp.run(module, {"x": xs}, consts, batch=True)
     cm = anvil.compile(module, consts=consts, prove=False, params=CudaParams(checked=checked))
