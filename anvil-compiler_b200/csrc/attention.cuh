@@ -129,6 +129,17 @@ __device__ __forceinline__ int attn_item(int k, int ntiles) {
   return t < ntiles ? t : -1;
 }
 
+// ceil(2^(31 + lg) / S) for 2 <= S < 2^31 and lg = ceil(log2 S) (below 2^32): the correctly rounded double quotient
+// is within 2^-21 of the true one, so its truncation + 1 is the ceiling or one off it, and the two exact 64-bit
+// checks below settle which. Cheaper, once per row and tile, than a 64-bit integer division.
+__device__ __forceinline__ unsigned ceil_pow2_div(int S, int lg) {
+  const unsigned long long N = 1ull << (31 + lg), s = (unsigned long long)S;
+  unsigned long long m = (unsigned long long)((double)N / (double)S) + 1ull;
+  if ((m - 1ull) * s >= N) --m;
+  if (m * s < N) ++m;
+  return (unsigned)m;
+}
+
 template <int HD>
 __global__ void __launch_bounds__(ATTN_THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
@@ -435,8 +446,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       // n doubled (one2 = 2*one, m = 2^31, shift 0): the high word of 2n * 2^31 is n (2n < 2^32 as e*one < 2^31).
       const int S = tot > 0 ? tot : 1;
       const int lg = S > 1 ? 32 - __clz(S - 1) : 0;
-      const unsigned magic =
-          S > 1 ? (unsigned)(((1ull << (31 + lg)) + (unsigned long long)(S - 1)) / (unsigned long long)S) : 0x80000000u;
+      const unsigned magic = S > 1 ? ceil_pow2_div(S, lg) : 0x80000000u;
       const int msh = lg > 0 ? lg - 1 : 0;
       const unsigned one2 = S > 1 ? (unsigned)p.one : 2u * (unsigned)p.one;
       const unsigned half2 = S > 1 ? (unsigned)(tot >> 1) : 2u * (unsigned)(tot >> 1);
