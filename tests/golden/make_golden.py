@@ -1,8 +1,8 @@
 """Generate the golden fixtures in tests/golden/ by EXECUTING the reference's own Python sources.
 
-Run in a container that has the reference checkout (default /root/reference, or $ANVIL_REFERENCE):
+Run where a checkout of the reference exists, with $ANVIL_REFERENCE naming its directory:
 
-    python tests/golden/make_golden.py
+    ANVIL_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 The reference's anvil package cannot be imported whole here (it needs xdsl and the missing xf submodule), but two
 of its modules run on numpy alone once their imports are satisfied:
@@ -34,7 +34,9 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(os.environ.get("ANVIL_REFERENCE", "/root/reference"))
+if not os.environ.get("ANVIL_REFERENCE"):
+    sys.exit("make_golden.py: set ANVIL_REFERENCE to the reference checkout's directory")
+REF = Path(os.environ["ANVIL_REFERENCE"])
 sys.path[:0] = [str(ROOT / "anvil-compiler_b200"), str(ROOT)]
 
 from oracle import semantics as osem  # noqa: E402
