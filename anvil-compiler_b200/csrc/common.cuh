@@ -242,6 +242,10 @@ __device__ __forceinline__ void st_shared_v4(void *p, uint32_t a, uint32_t b, ui
                : "memory");
 }
 
+__device__ __forceinline__ void st_shared_u32(void *p, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void st_shared_u8(void *p, uint32_t v) {
   asm volatile("st.shared.u8 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
 }

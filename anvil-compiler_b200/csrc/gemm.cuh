@@ -575,12 +575,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
           for (int q = 0; q < 4; ++q) w[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
           st_shared_v4(stg + ((sc ^ ((lane >> 1) & 3)) << 4), w[0], w[1], w[2], w[3]);
-        } else if (tmode == 2) {            // column q of the sub-chunk -> staging row sc*16 + q, this lane's byte
+        } else if (tmode == 2) {
+          // column c of the sub-chunk -> staging row sc*16 + c, byte = this lane's row. A 4 x 4 byte transpose
+          // inside each quad of lanes (rows 4g..4g+3) gives lane 4g+i, for each word q, column 4q+i of the quad's
+          // four rows as one word, stored at offset 4g (the banks 8i + g are all different)
+          const int qi = lane & 3;
+          const uint32_t sel1 = (qi & 1) ? 0x3715u : 0x6240u, sel2 = qi < 2 ? 0x5410u : 0x3276u;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const uint32_t w = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-#pragma unroll
-            for (int k2 = 0; k2 < 4; ++k2) st_shared_u8(stg_w + (sc * 16 + 4 * q + k2) * 32 + lane, w >> (8 * k2));
+            const uint32_t u = __byte_perm(w, __shfl_xor_sync(0xffffffffu, w, 1), sel1);
+            const uint32_t t = __byte_perm(u, __shfl_xor_sync(0xffffffffu, u, 2), sel2);
+            st_shared_u32(stg_w + (sc * 16 + 4 * q + qi) * 32 + 4 * (lane >> 2), t);
           }
         } else if (row_ok) {
           const int cnt = (int)(p.N - col0 < 16 ? p.N - col0 : 16);
@@ -611,7 +617,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (lane == 0 && row0 + lane_base < p.M) {    // a pair's odd CTA may have no rows left in the last tile
           const int64_t r0 = row0 + lane_base;
           const int c0 = (int)cbase;
-          if (tmode == 2) tma_store_3d(&tmC, stg_w, (int)(r0 % p.o_group), c0, (int)(r0 / p.o_group));
+          if (tmode == 2) {                            // r0 and the group (T) are below 2^31
+            const uint32_t grp = (uint32_t)p.o_group, gq = (uint32_t)r0 / grp;
+            tma_store_3d(&tmC, stg_w, (int)((uint32_t)r0 - gq * grp), c0, (int)gq);
+          }
           else if (p.batch > 1) tma_store_3d(&tmC, stg_w, c0, (int)r0, (int)bb);
           else tma_store_2d(&tmC, stg_w, c0, (int)r0);
           bulk_commit();
