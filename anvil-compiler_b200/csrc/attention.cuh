@@ -313,6 +313,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     int32_t *red_sum = red_max + 512;                                          // [4][128] partial row sum
     const int lcopy = lane % Cfg::LUT_COPIES;
     const long long rnd2 = round_term(p.s2);
+    const bool m2_32 = p.m2 >= 0 && p.m2 <= 0x7fffffffll && rnd2 <= 0x7fffffffll;
     uint32_t gs = 0;
     uint32_t fph = 0;                                // bit j: parity of P slab j's uses so far
     // O = P V of a finished tile: TMEM -> requant -> merged-heads output row. The last HD/32 parts take 32
@@ -328,8 +329,13 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(Cfg::O_COL + opart * 32), acc);
         uint32_t wq[8];
         int v[32];
+        if (m2_32) {                       // the static int32 proof bounds acc*M2 + 2^(s2-1): 32-bit, clamp in the pack
 #pragma unroll
-        for (int q = 0; q < 32; ++q) v[q] = (int)clampi(((long long)acc[q] * p.m2 + rnd2) >> p.s2, -128, 127);
+          for (int q = 0; q < 32; ++q) v[q] = (acc[q] * (int)p.m2 + (int)rnd2) >> p.s2;
+        } else {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) v[q] = (int)clampi(((long long)acc[q] * p.m2 + rnd2) >> p.s2, -128, 127);
+        }
 #pragma unroll
         for (int q = 0; q < 8; ++q) wq[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         if (row < p.T1) {
