@@ -30,6 +30,8 @@ from .ir import graph as g
 BACKENDS = ("cuda",)
 PIPELINE_MODELS = 4          # device models (arenas + streams) a pipelined run rotates over
 PIPELINE_TOKENS = 16384      # "auto" pipeline chunk size, in tokens
+NOMINAL_PEAKS = {"int8_tops": 4500.0, "hbm_gbs": 7700.0}    # B200 dense int8 tensor and HBM3e, NVIDIA's figures
+GUARD_BYTES = 256            # canary bytes after every buffer of a guarded (stray-write checked) run
 
 
 @dataclass(frozen=True)
@@ -38,7 +40,10 @@ class CudaParams:
 
     devices   CUDA device ordinals; a batch is sharded across them (contiguous, ceil(B / G) each)
     checked   check every int32 intermediate on the device (OverflowError like the oracle); None: only when
-              the static overflow proof does not hold for the graph
+              the static overflow proof does not hold for the graph. False on a graph the proof rejects runs the
+              unchecked 32-bit arithmetic anyway (with a RuntimeWarning): the outputs are then exact only on inputs
+              where no intermediate leaves int32, and where the oracle would raise OverflowError they are
+              unspecified
     fuse      apply launch fusions (LUT epilogues, fused attention); keep="all" runs disable them
     gemm      "auto" | "tc" (tcgen05 wherever the shape allows) | "simt" (CUDA-core kernel everywhere)
     pipeline  equal chunks a device's share of a run is split into, so one chunk's host<->device copies overlap
@@ -68,13 +73,25 @@ class RunOutput:
     in its graph dtype (int8 / int16 / int32); `output` / `outputs` are the dequantized graph outputs, computed
     on first access."""
 
-    def __init__(self, model, ints: dict, cycles: dict, result=None, job=None):
+    def __init__(self, model, ints: dict, cycles: dict, result=None, job=None, stray=None):
         self._model = model
         self.ints = ints                # sym -> int array of every value readable after the run
         self.cycles = cycles            # launch label -> device microseconds (None unless run(..., timing=True))
         self.result = result            # CudaRunResult
         self.job = job                  # the DeviceProgram of the first device
         self._outs = None
+        self._stray = stray             # guarded runs: [(device, region, byte offset)] the run must not have changed
+
+    def stray_writes(self, *, scratch_ok: bool = True) -> list:
+        """Bytes the run changed that it must not have (anvil/driver.py:66-71): outside every planned arena
+        buffer (alignment gaps, the canary after each buffer, past the plan) or anywhere in the const region
+        (weights, LUTs, biases), as (device, "arena" | "const", byte offset). Empty for a correct launch chain.
+        Needs a run(..., guard=True), which fills the arena with a canary pattern before the run and reads the
+        arena and the const region back after it. `scratch_ok` is accepted for the reference's signature: this
+        target has no shared scratch words."""
+        if self._stray is None:
+            raise ValueError("stray_writes() needs a run(..., guard=True): only a guarded run records the memory")
+        return list(self._stray)
 
     @property
     def outputs(self) -> list:
@@ -169,6 +186,11 @@ class CompiledModel:
                 proven = False
         self.proven = proven
         self.checked = (not proven) if self.params.checked is None else bool(self.params.checked)
+        if not self.checked and not proven:
+            import warnings
+            warnings.warn("checked=False on a graph whose static int32 proof fails: the outputs are exact only on "
+                          "inputs where no int32 intermediate overflows (where the oracle raises OverflowError they "
+                          "are unspecified)", RuntimeWarning, stacklevel=2)
         from .runtime.program import ConstPool
         self._pool = ConstPool()
         self._programs = {}          # (batch, keep) -> DeviceProgram
@@ -178,12 +200,15 @@ class CompiledModel:
         self._lock = threading.Lock()
 
     # ------------------------------------------------------------------------------------- programs
-    def program(self, batch: int = 1, keep: str = "outputs"):
+    def program(self, batch: int = 1, keep: str = "outputs", guard: bool = False):
+        """The launch list for `batch` samples (cached); guard=True gives the debug layout of a stray-write check
+        (no buffer reuse, GUARD_BYTES of canary after every buffer)."""
         from .runtime.program import lower_program
-        key = (int(batch), keep)
+        key = (int(batch), keep, bool(guard))
         if key not in self._programs:
             self._programs[key] = lower_program(self.module, self.consts, self._pool, batch, keep,
-                                                checked=self.checked, fuse=self.params.fuse, gemm=self.params.gemm)
+                                                checked=self.checked, fuse=self.params.fuse, gemm=self.params.gemm,
+                                                guard=GUARD_BYTES if guard else 0)
         return self._programs[key]
 
     @property
@@ -327,11 +352,14 @@ class CompiledModel:
         return v
 
     # --------------------------------------------------------------------------------------------- runs
-    def run(self, x, backend: str = "cuda", *, quantized=False, keep="outputs", timing=False, out=None) -> RunOutput:
+    def run(self, x, backend: str = "cuda", *, quantized=False, keep="outputs", timing=False, out=None,
+            guard=False) -> RunOutput:
         """Quantize `x` (unless quantized=True), run the launch chain on the GPU(s), read back. `out` may map graph
         output syms to caller-owned C-contiguous arrays of the output's dtype and (batch,) + shape (pinned memory
         makes the read-back a DMA at full bus speed); those outputs are written there and returned as those
-        arrays."""
+        arrays. guard=True is a debug run for RunOutput.stray_writes(): the chain runs on the guarded layout (no
+        buffer reuse, canary bytes after every buffer) in one piece per device, and the arena and const region are
+        compared with what they held before."""
         if backend not in BACKENDS:
             raise ValueError(f"unknown backend {backend!r}: this build runs {', '.join(BACKENDS)} (the tiny-gpu "
                              "simulators isasim/rtl/verilator are not part of it)")
@@ -339,15 +367,15 @@ class CompiledModel:
             raise ValueError(f"keep must be 'outputs' or 'all', not {keep!r}")
         bound, batch, batched = self._bind_inputs(x, quantized)
         out = self._check_out(out, batch)
-        ints, kus, shards = self._run_cuda(bound, batch, keep, timing, out)
+        ints, kus, shards, stray = self._run_cuda(bound, batch, keep, timing, out, bool(guard))
         if not batched:
             ints = {k: v[0] if v.ndim and v.shape[0] == 1 and k not in self._const_syms() else v
                     for k, v in ints.items()}
-        prog = self.program(shards[0][1], keep)
+        prog = self.program(shards[0][1], keep, bool(guard))
         cycles = {}
         for d, us in zip(prog.devops, kus if kus is not None else [None] * len(prog.devops)):
             cycles[d.label] = (cycles.get(d.label) or 0) + us if us is not None else None
-        return RunOutput(self, ints, cycles, CudaRunResult(batch, shards, cycles), prog)
+        return RunOutput(self, ints, cycles, CudaRunResult(batch, shards, cycles), prog, stray)
 
     def _check_out(self, out, batch):
         if not out:
@@ -378,20 +406,20 @@ class CompiledModel:
             lo = hi
         return out
 
-    def _run_cuda(self, bound, batch, keep, timing, out=None):
+    def _run_cuda(self, bound, batch, keep, timing, out=None, guard=False):
         shards = self._shards(batch)
         results, errors = [None] * len(shards), [None] * len(shards)
 
         def work(i, dev, lo, hi):
             try:
                 results[i] = self._run_shard(dev, {k: v[lo:hi] for k, v in bound.items()}, hi - lo, keep, timing,
-                                             {k: v[lo:hi] for k, v in (out or {}).items()})
+                                             {k: v[lo:hi] for k, v in (out or {}).items()}, guard)
             except BaseException as e:            # re-raised on the calling thread
                 errors[i] = e
 
         with self._lock:
             for b in {hi - lo for _, lo, hi in shards}:        # lower (and pack consts) before any upload
-                self.program(b, keep)
+                self.program(b, keep, guard)
             if len(shards) == 1:
                 work(0, *shards[0])
             else:
@@ -410,16 +438,23 @@ class CompiledModel:
                 continue
             parts = [r[0][k] for r in results]
             ints[k] = parts[0] if k in self._const_syms() or len(parts) == 1 else np.concatenate(parts, axis=0)
-        return ints, results[0][1], [(d, hi - lo) for d, lo, hi in shards]
+        stray = None
+        if guard:
+            stray = [(d, region, off) for (d, _, _), r in zip(shards, results) for region, off in r[2]]
+        return ints, results[0][1], [(d, hi - lo) for d, lo, hi in shards], stray
 
-    def _run_shard(self, device, bound, b, keep, timing, out=None):
-        plan = self._chunk_plan(b, keep, timing)
+    def _run_shard(self, device, bound, b, keep, timing, out=None, guard=False):
+        plan = [b] if guard else self._chunk_plan(b, keep, timing)
         if len(plan) > 1 and all(self._pipelinable(self.program(c, keep)) for c in set(plan)):
-            return self._run_pipelined(device, bound, b, plan, out)
-        prog = self.program(b, keep)
+            return self._run_pipelined(device, bound, b, plan, out) + (None,)
+        prog = self.program(b, keep, guard)
         dm = self._device_model(device)
-        if dm.prepared_key != (b, keep):
-            dm.prepare(prog.ops, prog.plan.arena, key=(b, keep))
+        if dm.prepared_key != (b, keep, guard):
+            dm.prepare(prog.ops, prog.plan.arena, key=(b, keep, guard))
+        canary = None
+        if guard:
+            canary = canary_bytes(prog.plan.arena)
+            dm.write(0, canary)
         ins = []
         for sym, (off, shape, dtype) in prog.inputs.items():
             arr = np.ascontiguousarray(bound[sym], dtype={"i8": np.int8, "i16": np.int16, "i32": np.int32}[dtype])
@@ -437,6 +472,11 @@ class CompiledModel:
             roots[r] = buf
             outs.append((prog.plan.addresses[r], buf))
         kus = dm.run(ins, outs, timing=timing)
+        stray = None
+        if guard:
+            after = dm.read(0, np.empty(prog.plan.arena, dtype=np.uint8))
+            consts_after = dm.read_const(0, np.empty(self._pool.size, dtype=np.uint8))
+            stray = stray_bytes(prog.plan.inside(), canary, after, self._pool.blob(), consts_after)
         ints = dict(direct)
         for sym, v in want.items():
             if sym in direct:
@@ -447,7 +487,7 @@ class CompiledModel:
                 ints[sym] = out[sym]
         for sym in self.inputs:
             ints.setdefault(sym, bound[sym])
-        return ints, kus
+        return ints, kus, stray
 
     def _pipelinable(self, prog) -> bool:
         """Every graph output is a whole, contiguous arena buffer (copied per chunk straight into its rows)."""
@@ -521,24 +561,68 @@ class CompiledModel:
         return list(self._readable(prog, keep)) + [s for s in self.inputs]
 
     # ------------------------------------------------------------------------------------------ summary
-    def summary(self, batch: int = 1, kernel_us: dict | None = None) -> str:
-        """Per launch: label, kernel, shape, algorithmic ops / bytes (and measured us when given), then the plan."""
-        from .runtime.cuda import KIND_NAMES
+    def summary(self, batch: int = 1, kernel_us: dict | None = None, peaks: dict | None = None) -> str:
+        """Per launch: label, kernel, shape, algorithmic ops / bytes; with `kernel_us` (RunOutput.cycles of a
+        timing=True run, label -> device us) the achieved rate and its fraction of the roofline that bounds the
+        kernel (ops against the dense int8 tensor peak, bytes against HBM bandwidth); then the fusions and the plan
+        (the reference's summary, anvil/driver.py:324-327). `peaks` = {"int8_tops": ..., "hbm_gbs": ...} gives the
+        denominators (default: B200 nominal, 4500 dense int8 TOP/s and 7700 GB/s). When the first device's model
+        is prepared for this batch, each launch also shows the tile shape the library chose."""
+        from .runtime.cuda import KIND_NAMES, OP_ATTENTION, OP_GEMM
+        pk = dict(NOMINAL_PEAKS, **(peaks or {}))
         prog = self.program(batch)
+        dm = self._devices.get(self.params.devices[0])
+        shapes = dm is not None and dm.prepared_key == (batch, "outputs", False)
         rows = []
         for i, d in enumerate(prog.devops):
             f = d.fields
             kname = KIND_NAMES.get(d.kind, str(d.kind))
-            if d.kind == 1:
+            if d.kind == OP_GEMM:
                 kname += "[simt]" if f.get("flags", 0) & 32 else "[tcgen05]"
             dims = "x".join(str(v) for v in f.get("dims", []))
             w = d.work
             work = (f"{w['ops'] / 1e6:10.2f} Mop" if "ops" in w else f"{w.get('bytes', 0) / 1e6:10.2f} MB ")
-            t = "" if not kernel_us or d.label not in kernel_us else f" {kernel_us[d.label]:9.2f} us"
-            rows.append(f"{d.label:>16} {kname:<18} {dims:<24} {work}{t}")
+            shape = ""
+            if shapes and d.kind in (OP_GEMM, OP_ATTENTION):
+                a, b, tiles, ctas = dm.describe(i)
+                if d.kind == OP_GEMM:
+                    shape = f" [{'pair ' if b == 2 else ''}BN {a}, {tiles} tiles, {ctas} CTAs]" if a else \
+                        f" [{tiles} blocks]"
+                else:
+                    shape = f" [{tiles} items, {ctas} CTAs]"
+            t = ""
+            if kernel_us and d.label in kernel_us and kernel_us[d.label]:
+                us = kernel_us[d.label]
+                if "ops" in w:
+                    rate = w["ops"] / (us * 1e-6) / 1e12
+                    t = f" {us:9.2f} us {rate:8.1f} TOP/s {rate / pk['int8_tops']:6.1%} of int8"
+                else:
+                    rate = w.get("bytes", 0) / (us * 1e-6) / 1e9
+                    t = f" {us:9.2f} us {rate:8.1f} GB/s  {rate / pk['hbm_gbs']:6.1%} of HBM"
+            rows.append(f"{d.label:>16} {kname:<18} {dims:<24} {work}{t}{shape}")
         extra = [f"fusions: {', '.join(prog.fused) or 'none'}", f"checked: {self.checked} (proof "
                  f"{'holds' if self.proven else 'fails'})", prog.plan.report()]
+        if kernel_us:
+            extra.append(f"roofline denominators: {pk['int8_tops']} int8 TOP/s, {pk['hbm_gbs']} GB/s")
         return "\n".join(rows + extra)
+
+
+def canary_bytes(n: int) -> np.ndarray:
+    """The canary a guarded run fills the arena with: n pseudo-random bytes from a fixed seed (no constant byte
+    value that a kernel might happen to write)."""
+    return np.random.default_rng(0xA5C0FFEE).integers(0, 256, n, dtype=np.uint8)
+
+
+def stray_bytes(inside: np.ndarray, canary: np.ndarray, after: np.ndarray, blob: np.ndarray,
+                consts_after: np.ndarray) -> list:
+    """[("arena" | "const", byte offset)] of the bytes a run changed that it must not have: arena bytes outside
+    every planned buffer (`inside` False) that no longer hold the canary, and const bytes that differ from the
+    uploaded blob (the reference's JobPlan.stray_writes, anvil/codegen/__init__.py:150-168, in bytes)."""
+    n = min(len(inside), len(after), len(canary))
+    arena = np.flatnonzero((after[:n] != canary[:n]) & ~inside[:n])
+    m = min(len(blob), len(consts_after))
+    const = np.flatnonzero(np.asarray(consts_after[:m]) != np.asarray(blob[:m]))
+    return [("arena", int(o)) for o in arena] + [("const", int(o)) for o in const]
 
 
 def _apply_view(buf: np.ndarray, v) -> np.ndarray:

@@ -33,114 +33,202 @@ class UnsupportedOpError(NotImplementedError):
     """An op (or a use of an op) outside the frontend's patterns; the message names the ATen op."""
 
 
-@dataclass(eq=False)
 class FNode:
-    op: str
-    name: str
-    inputs: list
-    attrs: dict
-    shape: tuple                      # per-sample shape (no batch dim)
+    """One frontend op: `op` (the op set in the module docstring), a unique `name`, its operand nodes `inputs`,
+    op attributes `attrs` (weights as float64 numpy arrays) and the per-sample result `shape` (no batch dim).
+    Nodes compare by identity: two nodes with the same fields are still two values."""
+
+    __slots__ = ("op", "name", "inputs", "attrs", "shape")
+
+    def __init__(self, op: str, name: str, inputs, attrs: dict, shape):
+        self.op, self.name, self.inputs = op, name, list(inputs)
+        self.attrs, self.shape = dict(attrs), tuple(shape)
 
     def __repr__(self):
         return f"FNode({self.op} {self.name} {list(self.shape)})"
 
 
-@dataclass
 class FGraph:
-    nodes: list
-    inputs: list
-    outputs: list
-    batch: int = 1
+    """A captured float graph: `nodes` in evaluation order, the `inputs` and `outputs` among them, and the
+    example batch size. Lookups by name and the users of a node come from indexes built on first use (the graph
+    is not changed after capture)."""
+
+    def __init__(self, nodes, inputs, outputs, batch: int = 1):
+        self.nodes, self.inputs, self.outputs, self.batch = list(nodes), list(inputs), list(outputs), batch
+        self._by_name = None
+        self._users = None
 
     def node(self, name) -> FNode:
-        for n in self.nodes:
-            if n.name == name:
-                return n
-        raise KeyError(name)
+        if self._by_name is None:
+            self._by_name = {n.name: n for n in self.nodes}
+        return self._by_name[name]
 
     def users(self, node) -> list:
-        return [n for n in self.nodes if any(i is node for i in n.inputs)]
+        """The nodes that read `node`, in evaluation order (once each)."""
+        if self._users is None:
+            idx = {}
+            for n in self.nodes:
+                for i in {id(x): x for x in n.inputs}.values():
+                    idx.setdefault(id(i), []).append(n)
+            self._users = idx
+        return list(self._users.get(id(node), ()))
 
     def text(self) -> str:
-        lines = []
-        for n in self.nodes:
-            ins = ", ".join(i.name for i in n.inputs)
-            attrs = ", ".join(f"{k}={_fmt(v)}" for k, v in sorted(n.attrs.items()))
-            lines.append(f"{n.name} = {n.op}({ins}) {{{attrs}}} : {list(n.shape)}")
-        lines.append("return " + ", ".join(o.name for o in self.outputs))
-        return "\n".join(lines) + "\n"
+        def attr_text(at):
+            return ", ".join(f"{k}={_fmt(at[k])}" for k in sorted(at))
+        body = [f"{n.name} = {n.op}({', '.join(i.name for i in n.inputs)}) {{{attr_text(n.attrs)}}} : "
+                f"{list(n.shape)}" for n in self.nodes]
+        return "\n".join(body + ["return " + ", ".join(o.name for o in self.outputs)]) + "\n"
 
-    def evaluate(self, inputs) -> dict:
-        """Float64 activations {node name: torch tensor} on batched inputs (dict by input name, or a sequence)."""
+    def evaluate(self, inputs, observe=None, keep_all: bool = True) -> dict:
+        """Float64 activations {node name: torch tensor} on batched inputs (a dict by input name, or a sequence in
+        input order). `observe(node, tensor)` is called as each value is computed; with keep_all=False a value is
+        dropped once its last reader has run (graph outputs are kept), so a calibration pass that only observes
+        holds a few activations at a time."""
         import torch
-        import torch.nn.functional as F
 
         if not isinstance(inputs, dict):
             inputs = {n.name: x for n, x in zip(self.inputs, inputs, strict=True)}
+        last_read = {}
+        if not keep_all:
+            for pos, n in enumerate(self.nodes):
+                for i in n.inputs:
+                    last_read[i.name] = pos
+            for o in self.outputs:
+                last_read[o.name] = len(self.nodes)
         env = {}
-        for n in self.nodes:
-            a = [env[i.name] for i in n.inputs]
-            at = n.attrs
-            if n.op == "input":
-                v = torch.as_tensor(inputs[n.name])
-                v = v.long() if at.get("ids") else v.to(torch.float64)
-            elif n.op == "embed":
-                ids = a[0]
-                wte = torch.as_tensor(at["wte"], dtype=torch.float64)
-                v = wte[ids]
-                if at["wpe"] is not None:
-                    v = v + torch.as_tensor(at["wpe"], dtype=torch.float64)[: ids.shape[-1]]
-            elif n.op == "layernorm":
-                w = None if at["weight"] is None else torch.as_tensor(at["weight"], dtype=torch.float64)
-                b = None if at["bias"] is None else torch.as_tensor(at["bias"], dtype=torch.float64)
-                v = F.layer_norm(a[0], (a[0].shape[-1],), w, b, at["eps"])
-            elif n.op == "rmsnorm":
-                x = a[0]
-                v = x * (x.pow(2).mean(dim=-1, keepdim=True) + at["eps"]).rsqrt()
-                if at["weight"] is not None:
-                    v = v * torch.as_tensor(at["weight"], dtype=torch.float64)
-            elif n.op == "linear":
-                w = torch.as_tensor(at["weight"], dtype=torch.float64)
-                b = None if at["bias"] is None else torch.as_tensor(at["bias"], dtype=torch.float64)
-                if at["rows"] is not None:
-                    lo, hi = at["rows"]
-                    w = w[lo:hi]
-                    b = None if b is None else b[lo:hi]
-                v = F.linear(a[0], w, b)
-            elif n.op == "matmul":
-                v = torch.matmul(a[0], a[1])
-                f = at["factor"]
-                if f is not None:
-                    v = v / math.sqrt(f[1]) if f[0] == "inv_sqrt" else v * f[1]
-            elif n.op == "softmax":
-                x = a[0]
-                if at["causal"]:
-                    keep = torch.ones(x.shape[-2], x.shape[-1], dtype=torch.bool).tril()
-                    x = x.masked_fill(~keep, float("-inf"))
-                v = F.softmax(x, dim=-1)
-            elif n.op == "gelu":
-                v = F.gelu(a[0], approximate=at["approximate"])
-            elif n.op == "silu":
-                v = F.silu(a[0])
-            elif n.op == "mul":
-                v = a[0] * a[1]
-            elif n.op == "add":
-                v = a[0] + a[1]
-            elif n.op == "transpose":
-                nb = a[0].dim() - len(at["perm"])
-                v = a[0].permute(*range(nb), *(nb + p for p in at["perm"]))
-            elif n.op == "reshape":
-                v = a[0].reshape(*a[0].shape[:a[0].dim() - len(n.inputs[0].shape)], *n.shape)
-            elif n.op == "split_heads":
-                x = a[0]
-                v = x.reshape(*x.shape[:-1], at["nh"], x.shape[-1] // at["nh"]).transpose(-3, -2)
-            elif n.op == "merge_heads":
-                x = a[0].transpose(-3, -2)
-                v = x.reshape(*x.shape[:-2], x.shape[-2] * x.shape[-1])
-            else:
-                raise NotImplementedError(n.op)
-            env[n.name] = v
+        with torch.no_grad():
+            for pos, n in enumerate(self.nodes):
+                rule = _FLOAT_RULES.get(n.op)
+                if rule is None:
+                    raise NotImplementedError(f"no float semantics for frontend op {n.op!r}")
+                v = rule(n, [env[i.name] for i in n.inputs], inputs)
+                env[n.name] = v
+                if observe is not None:
+                    observe(n, v)
+                if not keep_all:
+                    for i in {x.name for x in n.inputs}:
+                        if last_read.get(i, -1) <= pos:
+                            env.pop(i, None)
+                    if last_read.get(n.name, -1) < pos:
+                        env.pop(n.name, None)
         return env
+
+
+# ------------------------------------------------------------------------------------- float semantics
+# One function per frontend op: (node, operand tensors, graph inputs) -> float64 result, batched on the leading
+# dim. These define what the quantized graph approximates (its activations calibrate the scales, and the
+# float-path tolerance is measured against them).
+
+def _t64(a):
+    import torch
+    return None if a is None else torch.as_tensor(a, dtype=torch.float64)
+
+
+def _f_input(n, a, inputs):
+    import torch
+    v = torch.as_tensor(inputs[n.name])
+    return v.long() if n.attrs.get("ids") else v.to(torch.float64)
+
+
+def _f_embed(n, a, inputs):
+    ids = a[0]
+    v = _t64(n.attrs["wte"])[ids]
+    pos = n.attrs["wpe"]
+    return v if pos is None else v + _t64(pos)[: ids.shape[-1]]
+
+
+def _f_layernorm(n, a, inputs):
+    import torch.nn.functional as F
+    x = a[0]
+    return F.layer_norm(x, (x.shape[-1],), _t64(n.attrs["weight"]), _t64(n.attrs["bias"]), n.attrs["eps"])
+
+
+def _f_rmsnorm(n, a, inputs):
+    x = a[0]
+    v = x * (x.pow(2).mean(dim=-1, keepdim=True) + n.attrs["eps"]).rsqrt()
+    w = n.attrs["weight"]
+    return v if w is None else v * _t64(w)
+
+
+def _f_linear(n, a, inputs):
+    import torch.nn.functional as F
+    w, b, rows = _t64(n.attrs["weight"]), _t64(n.attrs["bias"]), n.attrs["rows"]
+    if rows is not None:
+        w = w[rows[0]:rows[1]]
+        b = None if b is None else b[rows[0]:rows[1]]
+    return F.linear(a[0], w, b)
+
+
+def _f_matmul(n, a, inputs):
+    import torch
+    v = torch.matmul(a[0], a[1])
+    f = n.attrs["factor"]
+    if f is None:
+        return v
+    return v / math.sqrt(f[1]) if f[0] == "inv_sqrt" else v * f[1]
+
+
+_CAUSAL_BIAS = {}
+
+
+def _causal_bias(t1, t2):
+    """(t1, t2) float64: 0 where row i keeps column j (j <= i), -inf elsewhere (cached per shape)."""
+    import torch
+    key = (t1, t2)
+    if key not in _CAUSAL_BIAS:
+        _CAUSAL_BIAS[key] = torch.zeros(t1, t2, dtype=torch.float64).masked_fill(
+            torch.ones(t1, t2, dtype=torch.bool).triu(1), float("-inf"))
+    return _CAUSAL_BIAS[key]
+
+
+def _f_softmax(n, a, inputs):
+    import torch.nn.functional as F
+    x = a[0]
+    if n.attrs["causal"]:
+        x = x + _causal_bias(x.shape[-2], x.shape[-1])        # adding 0 leaves kept scores exact
+    return F.softmax(x, dim=-1)
+
+
+def _f_gelu(n, a, inputs):
+    import torch.nn.functional as F
+    return F.gelu(a[0], approximate=n.attrs["approximate"])
+
+
+def _f_silu(n, a, inputs):
+    import torch.nn.functional as F
+    return F.silu(a[0])
+
+
+def _f_transpose(n, a, inputs):
+    x, perm = a[0], n.attrs["perm"]
+    lead = x.dim() - len(perm)
+    return x.permute(*range(lead), *(lead + p for p in perm))
+
+
+def _f_reshape(n, a, inputs):
+    x = a[0]
+    lead = x.dim() - len(n.inputs[0].shape)
+    return x.reshape(*x.shape[:lead], *n.shape)
+
+
+def _f_split_heads(n, a, inputs):
+    x, nh = a[0], n.attrs["nh"]
+    return x.reshape(*x.shape[:-1], nh, x.shape[-1] // nh).transpose(-3, -2)
+
+
+def _f_merge_heads(n, a, inputs):
+    x = a[0].transpose(-3, -2)
+    return x.reshape(*x.shape[:-2], x.shape[-2] * x.shape[-1])
+
+
+_FLOAT_RULES = {
+    "input": _f_input, "embed": _f_embed, "layernorm": _f_layernorm, "rmsnorm": _f_rmsnorm,
+    "linear": _f_linear, "matmul": _f_matmul, "softmax": _f_softmax, "gelu": _f_gelu, "silu": _f_silu,
+    "mul": lambda n, a, inputs: a[0] * a[1], "add": lambda n, a, inputs: a[0] + a[1],
+    "transpose": _f_transpose, "reshape": _f_reshape, "split_heads": _f_split_heads,
+    "merge_heads": _f_merge_heads,
+}
 
 
 def _fmt(v):

@@ -42,6 +42,17 @@ class MemPlan:
     bufs: dict                                  # sym -> Buf
     arena: int = 0                              # arena bytes
     const_bytes: int = 0
+    guard: int = 0                              # guarded plan: bytes of canary after every buffer (no reuse)
+
+    def inside(self) -> "np.ndarray":
+        """Boolean mask over the arena's bytes: True where some planned buffer lives (the bytes a correct launch
+        chain may change); everything else is alignment gap or guard."""
+        import numpy as np
+        m = np.zeros(self.arena, dtype=bool)
+        for s, b in self.bufs.items():
+            a = self.addresses[s]
+            m[a:a + b.size] = True
+        return m
 
     @property
     def unshared(self) -> int:
@@ -53,8 +64,9 @@ class MemPlan:
         return self.arena + self.const_bytes
 
     def report(self) -> str:
+        g = f"; guarded, {self.guard} canary bytes after every buffer" if self.guard else ""
         return (f"footprint {self.footprint} bytes (consts {self.const_bytes}, activations {self.arena}; "
-                f"activations without reuse {self.unshared})")
+                f"activations without reuse {self.unshared}{g})")
 
 
 def _align(n: int, a: int = ALIGN) -> int:
@@ -77,6 +89,16 @@ def assign_offsets(bufs, align: int = ALIGN) -> tuple[dict, int]:
         out[b.sym] = off
         placed.append((off, b))
         top = max(top, off + size)
+    return out, top
+
+
+def assign_guarded(bufs, guard: int, align: int = ALIGN) -> tuple[dict, int]:
+    """({sym: offset}, arena bytes) for a debug run: every buffer its own bytes (no reuse), each followed by at
+    least `guard` bytes that belong to no buffer, so a store past any buffer's end lands in a guard region."""
+    out, top = {}, 0
+    for b in sorted(bufs, key=lambda b: (b.start, b.sym)):
+        out[b.sym] = top
+        top = _align(top + b.size + guard, align)
     return out, top
 
 
@@ -111,10 +133,11 @@ def liveness(n_ops: int, sizes: dict, defs: dict, uses: dict, inputs, outputs, k
 
 
 def plan(n_ops: int, sizes: dict, defs: dict, uses: dict, inputs, outputs, keep="outputs", const_bytes=0,
-         max_bytes: int | None = None) -> MemPlan:
+         max_bytes: int | None = None, guard: int = 0) -> MemPlan:
+    """The liveness plan; with `guard` > 0 the debug layout of assign_guarded instead (stray-write checks)."""
     bufs = liveness(n_ops, sizes, defs, uses, inputs, outputs, keep)
-    offs, arena = assign_offsets(bufs.values())
-    mp = MemPlan(offs, bufs, arena, const_bytes)
+    offs, arena = assign_guarded(bufs.values(), guard) if guard else assign_offsets(bufs.values())
+    mp = MemPlan(offs, bufs, arena, const_bytes, guard)
     if max_bytes is not None and mp.footprint > max_bytes:
         raise MemoryPlanError(f"plan needs {mp.footprint} bytes > {max_bytes}: " + mp.report())
     bad = check_disjoint(bufs.values(), offs)

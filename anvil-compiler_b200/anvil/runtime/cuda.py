@@ -30,7 +30,9 @@ KIND_NAMES = {OP_GEMM: "gemm", OP_LUT: "lut", OP_LUT_MUL: "lut_mul", OP_ADD_REQU
 EXPORTS = ("anvil_abi_version", "anvil_last_error", "anvil_device_count", "anvil_cuda_init", "anvil_model_create",
            "anvil_model_prepare", "anvil_model_run", "anvil_model_enqueue", "anvil_model_clear_flags",
            "anvil_model_wait", "anvil_model_selftest_timeout", "anvil_model_run_device", "anvil_model_read",
-           "anvil_model_write", "anvil_model_arena", "anvil_model_free", "anvil_gemm_requant")
+           "anvil_model_write", "anvil_model_read_const", "anvil_model_arena", "anvil_model_describe",
+           "anvil_model_free",
+           "anvil_gemm_requant")
 
 
 class AnvilOp(ctypes.Structure):
@@ -77,7 +79,9 @@ def load_library(path: str | os.PathLike | None = None):
             "anvil_model_selftest_timeout": ([vp, u64], i32),
             "anvil_model_read": ([vp, u64, vp, u64], i32),
             "anvil_model_write": ([vp, u64, vp, u64], i32),
+            "anvil_model_read_const": ([vp, u64, vp, u64], i32),
             "anvil_model_arena": ([vp, ctypes.POINTER(u64), ctypes.POINTER(u64)], i32),
+            "anvil_model_describe": ([vp, i32, ctypes.POINTER(i64)], i32),
             "anvil_model_free": ([vp], None),
             "anvil_gemm_requant": ([vp, vp, vp, i64, i64, i64, ctypes.c_int32, ctypes.c_int32, u32, vp], i32),
         }
@@ -166,9 +170,21 @@ class DeviceModel:
         check(self.lib.anvil_model_read(self._h, int(offset), out.ctypes.data, out.nbytes), "anvil_model_read")
         return out
 
+    def read_const(self, offset: int, out: np.ndarray):
+        check(self.lib.anvil_model_read_const(self._h, int(offset), out.ctypes.data, out.nbytes),
+              "anvil_model_read_const")
+        return out
+
     def write(self, offset: int, data: np.ndarray):
         data = np.ascontiguousarray(data)
         check(self.lib.anvil_model_write(self._h, int(offset), data.ctypes.data, data.nbytes), "anvil_model_write")
+
+    def describe(self, op: int) -> tuple[int, int, int, int]:
+        """The launch shape of prepared op `op` (anvil_model_describe): GEMM (BN, CTAs per tile, tiles, CTAs),
+        attention (hd, 0, work items, CTAs), zeros otherwise."""
+        info = (ctypes.c_int64 * 4)()
+        check(self.lib.anvil_model_describe(self._h, int(op), info), "anvil_model_describe")
+        return tuple(int(v) for v in info)
 
     def pointers(self) -> tuple[int, int]:
         a, c = ctypes.c_uint64(0), ctypes.c_uint64(0)

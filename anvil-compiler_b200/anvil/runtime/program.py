@@ -603,7 +603,7 @@ class Lowering:
 
 
 def lower_program(module, consts: dict, pool: ConstPool, batch: int, keep="outputs", checked=False, fuse=True,
-                  gemm="auto") -> DeviceProgram:
+                  gemm="auto", guard: int = 0) -> DeviceProgram:
     L = Lowering(module, consts, pool, batch, keep, checked, fuse, gemm)
     L.run()
     func = L.func
@@ -635,7 +635,7 @@ def lower_program(module, consts: dict, pool: ConstPool, batch: int, keep="outpu
         if b not in defs and b not in input_bufs:
             del sizes[b]
     plan = memplan.plan(len(L.devops), sizes, defs, uses, input_bufs, keep_roots, "outputs",
-                        const_bytes=pool.size)
+                        const_bytes=pool.size, guard=guard)
     ops = []
     for i, d in enumerate(L.devops):
         o = C.AnvilOp()

@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -199,11 +200,62 @@ extern "C" int anvil_model_create(int device, const void *consts, uint64_t const
   return ANVIL_OK;
 }
 
-// Opt every large-shared-memory kernel in to its dynamic shared memory size on `device` (current), once.
-static int kernel_attrs(int device) {
-  static bool attrs[64] = {};     // the attribute is per function and per device
-  if (device >= 64) return fail(ANVIL_E_BAD_ARG, "device %d out of range", device);
-  if (!attrs[device]) {
+// Per-device facts every entry point needs, set up once per device (std::call_once: host threads that make
+// their first call on one device at the same time wait for a single set-up): the kernels' shared-memory opt-in
+// (a per-function, per-device attribute), the SM count and how many CTA pairs of the pair GEMM fit at once.
+struct DeviceInfo {
+  std::once_flag once;
+  int rc = ANVIL_OK;
+  std::string err;
+  int sms = 0;
+  int pair_capacity = 0;
+};
+static DeviceInfo g_dev_info[64];
+
+static int set_kernel_attrs();
+
+// The set-up of `device`, which must be the current device. Returns its status (the first failure is kept).
+static int device_info(int device, DeviceInfo **out) {
+  if (device < 0 || device >= 64) return fail(ANVIL_E_BAD_ARG, "device %d out of range", device);
+  DeviceInfo &d = g_dev_info[device];
+  std::call_once(d.once, [&]() {
+    int rc = set_kernel_attrs();
+    if (!rc && cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+      rc = fail(ANVIL_E_CUDA, "cannot read the SM count of device %d", device);
+    if (!rc) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      cfg.gridDim = dim3((unsigned)(d.sms & ~1));
+      cfg.blockDim = dim3(TC_THREADS);
+      cfg.dynamicSmemBytes = TcCfg<256, true>::SMEM_BYTES;
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&d.pair_capacity, qgemm_tc_kernel<256, 1, false, true>, &cfg) !=
+          cudaSuccess) {
+        cudaGetLastError();
+        d.pair_capacity = 0;
+      }
+    }
+    d.rc = rc;
+    if (rc) d.err = g_err;
+  });
+  if (d.rc) {
+    g_err = d.err;
+    return d.rc;
+  }
+  if (out) *out = &d;
+  return ANVIL_OK;
+}
+
+static int kernel_attrs(int device) { return device_info(device, nullptr); }
+
+// Opt every large-shared-memory kernel in to its dynamic shared memory size on the current device.
+static int set_kernel_attrs() {
+  {
     int r = 0;
     r |= set_smem(attn_kernel<64>, AttnCfg<64>::SMEM_BYTES);
     r |= set_smem(attn_kernel<128>, AttnCfg<128>::SMEM_BYTES);
@@ -218,7 +270,6 @@ static int kernel_attrs(int device) {
     TC_PAIR_ATTR(1) TC_PAIR_ATTR(2)
 #undef TC_PAIR_ATTR
     if (r) return ANVIL_E_CUDA;
-    attrs[device] = true;
   }
   return ANVIL_OK;
 }
@@ -276,22 +327,47 @@ static cudaLaunchConfig_t pair_config(dim3 grid, cudaStream_t st, cudaLaunchAttr
 }
 
 // How many CTA pairs of the pair GEMM fit on the device at once (0 turns the pair path off; so does
-// ANVIL_GEMM_PAIR=0 in the environment).
+// ANVIL_GEMM_PAIR=0 in the environment, read once per model).
 static int pair_clusters(anvil_model *m) {
   if (m->pair_clusters < 0) {
     const char *env = getenv("ANVIL_GEMM_PAIR");
-    int n = 0;
-    if (!env || atoi(env) != 0) {
-      cudaLaunchAttribute attr[1];
-      cudaLaunchConfig_t cfg = pair_config(dim3((unsigned)(m->sms & ~1)), m->stream, attr);
-      if (cudaOccupancyMaxActiveClusters(&n, qgemm_tc_kernel<256, 1, false, true>, &cfg) != cudaSuccess) {
-        cudaGetLastError();
-        n = 0;
-      }
-    }
-    m->pair_clusters = n;
+    DeviceInfo *di = nullptr;
+    m->pair_clusters = (env && atoi(env) == 0) || device_info(m->device, &di) ? 0 : di->pair_capacity;
   }
   return m->pair_clusters;
+}
+
+// The tile shape of a tcgen05 GEMM launch: BN (64, 128 or 256 output columns per tile) and single-CTA 128-row
+// tiles or 256-row tiles on CTA pairs (BN = 256 only). A persistent launch runs ceil(tiles / resident tiles)
+// rounds, and every SM of a round does 128 x BN x K MACs, so the time is about rounds x BN x K, weighted by how
+// efficiently each shape keeps the tensor pipe busy (measured on the c3 GEMMs: a single-CTA 256-column tile takes
+// about 1.1 x the pair's time per MAC; narrower tiles re-read A for fewer columns per MMA). The cheapest shape
+// wins, ties going to wider tiles. A fused residual epilogue over a short K is bound by its residual reads and
+// keeps single-CTA tiles (measured: 768 x 768 residual GEMM 58 us single, 60 us paired).
+struct TileChoice {
+  int bn;
+  bool pair;
+};
+
+static TileChoice choose_tiles(int64_t batch, int64_t M, int64_t N, int64_t K, int sms, int pair_cap, bool res) {
+  struct Cand { int bn; bool pair; double weight; };
+  const Cand cands[4] = {{256, true, 1.0}, {256, false, 1.1}, {128, false, 1.2}, {64, false, 1.45}};
+  TileChoice best = {256, false};
+  double best_cost = -1;
+  for (const Cand &c : cands) {
+    if (c.pair && (pair_cap <= 0 || M < 4 * TC_BM || (res && K < 2048) || N <= 128)) continue;
+    if (!c.pair && c.bn > 64 && N <= c.bn / 2) continue;            // a narrower tile holds every column
+    const int64_t rows = c.pair ? 2 * TC_BM : TC_BM;
+    const int64_t tiles = batch * ((M + rows - 1) / rows) * ((N + c.bn - 1) / c.bn);
+    const int64_t cap = c.pair ? pair_cap : sms;
+    const double rounds = (double)((tiles + cap - 1) / cap);
+    const double cost = rounds * c.bn * (double)K * c.weight;
+    if (best_cost < 0 || cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = {c.bn, c.pair};
+    }
+  }
+  return best;
 }
 
 
@@ -348,6 +424,26 @@ static int tile_magics(GemmParams &p, int op_index) {
   div_magic(p.n_tiles, &p.n_magic, &p.n_shift);
   div_magic(p.m_tiles, &p.m_magic, &p.m_shift);
   return ANVIL_OK;
+}
+
+// Tile shape, tile count, tile-decode magics and tensor maps of a tcgen05 GEMM whose GemmParams are filled in.
+static int tc_tiles(anvil_model *m, Launch &L) {
+  GemmParams &p = L.gp;
+  const TileChoice tc = choose_tiles(p.batch, p.M, p.N, p.K, m->sms, pair_clusters(m), p.res != nullptr);
+  L.bn = tc.bn;
+  L.pair = tc.pair;
+  const int64_t tile_rows = L.pair ? 2 * TC_BM : TC_BM;
+  p.m_tiles = (p.M + tile_rows - 1) / tile_rows;
+  p.n_tiles = (p.N + L.bn - 1) / L.bn;
+  p.tiles = p.batch * p.m_tiles * p.n_tiles;
+  int rc;
+  if ((rc = tile_magics(p, p.op_index))) return rc;
+  const int64_t M = p.M, N = p.N, K = p.K;
+  const uint64_t a_z = p.batch, a_zs = p.a_bstride ? p.a_bstride : M * K;
+  const uint64_t b_z = p.bt_bstride ? p.batch : 1, b_zs = p.bt_bstride ? p.bt_bstride : N * K;
+  if ((rc = make_map_i8(&L.mapA, p.A, K, M, a_z, K, a_zs, TC_BM))) return rc;
+  if ((rc = make_map_i8(&L.mapB, p.BT, K, N, b_z, K, b_zs, L.pair ? L.bn / 2 : L.bn))) return rc;
+  return gemm_out_map(L);
 }
 
 static int prepare_gemm(anvil_model *m, Launch &L) {
@@ -414,21 +510,7 @@ static int prepare_gemm(anvil_model *m, Launch &L) {
                      batch <= (1ll << 31) - 1;
   L.tc = tc_ok;
   if (!tc_ok) return ANVIL_OK;
-  L.bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
-  // wide outputs over many rows: 256-row tiles on CTA pairs, each SM staging half of every B tile, which relieves
-  // the shared-memory traffic of the main loop. A fused residual epilogue over a short K is bound by its own
-  // residual reads and keeps single-CTA tiles (measured: 768 x 768 residual GEMM 58 us single, 60 us paired).
-  L.pair = L.bn == 256 && M >= 4 * TC_BM && !(p.res && K < 2048) && pair_clusters(m) > 0;
-  const int64_t tile_rows = L.pair ? 2 * TC_BM : TC_BM;
-  p.m_tiles = (M + tile_rows - 1) / tile_rows;
-  p.n_tiles = (N + L.bn - 1) / L.bn;
-  p.tiles = batch * p.m_tiles * p.n_tiles;
-  if ((rc = tile_magics(p, op.op_index))) return rc;
-  const uint64_t a_z = batch, a_zs = a_bs ? a_bs : M * K;
-  const uint64_t b_z = bt_bs ? batch : 1, b_zs = bt_bs ? bt_bs : N * K;
-  if ((rc = make_map_i8(&L.mapA, p.A, K, M, a_z, K, a_zs, TC_BM))) return rc;
-  if ((rc = make_map_i8(&L.mapB, p.BT, K, N, b_z, K, b_zs, L.pair ? L.bn / 2 : L.bn))) return rc;
-  return gemm_out_map(L);
+  return tc_tiles(m, L);
 }
 
 // ATTENTION: dims = {B, H, T1, T2, hd}; strides = {q_b, q_h, q_t, k_b, k_h, k_t, o_b, o_t};
@@ -974,6 +1056,41 @@ extern "C" int anvil_model_write(anvil_model *m, uint64_t offset, const void *ho
   return ANVIL_OK;
 }
 
+extern "C" int anvil_model_read_const(anvil_model *m, uint64_t offset, void *host, uint64_t bytes) {
+  if (!m || !host) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_read_const");
+  if (offset > m->const_bytes || bytes > m->const_bytes - offset)
+    return fail(ANVIL_E_BAD_ARG, "read outside the const region");
+  CK(cudaSetDevice(m->device));
+  CK(cudaMemcpyAsync(host, static_cast<uint8_t *>(m->consts) + offset, bytes, cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  return ANVIL_OK;
+}
+
+extern "C" int anvil_model_describe(anvil_model *m, int op, int64_t *info) {
+  if (!m || !info || op < 0 || op >= (int)m->launches.size())
+    return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_describe");
+  const Launch &L = m->launches[op];
+  for (int i = 0; i < 4; ++i) info[i] = 0;
+  if (L.op.kind == ANVIL_OP_GEMM) {
+    const GemmParams &p = L.gp;
+    if (L.tc) {
+      info[0] = L.bn;
+      info[1] = L.pair ? 2 : 1;
+      info[2] = p.tiles;
+      info[3] = L.pair ? 2 * std::min<int64_t>(p.tiles, pair_clusters(m)) : std::min<int64_t>(p.tiles, m->sms);
+    } else {
+      info[2] = ((p.N + 63) / 64) * ((p.M + 63) / 64) * p.batch;
+      info[3] = info[2];
+    }
+  } else if (L.op.kind == ANVIL_OP_ATTENTION) {
+    const int64_t items = (int64_t)L.ap.B * L.ap.H * L.ap.nqt;
+    info[0] = L.hd;
+    info[2] = items;
+    info[3] = std::min<int64_t>(items, m->sms);
+  }
+  return ANVIL_OK;
+}
+
 extern "C" int anvil_model_arena(anvil_model *m, uint64_t *arena_ptr, uint64_t *const_ptr) {
   if (!m) return fail(ANVIL_E_BAD_ARG, "model is NULL");
   if (arena_ptr) *arena_ptr = reinterpret_cast<uint64_t>(m->arena);
@@ -983,30 +1100,24 @@ extern "C" int anvil_model_arena(anvil_model *m, uint64_t *arena_ptr, uint64_t *
 
 // ------------------------------------------------------------------------------------- standalone GEMM
 
-extern "C" int anvil_gemm_requant(const int8_t *A, const int8_t *BT, int8_t *out, int64_t M, int64_t N, int64_t K,
-                                  int32_t mult, int32_t shift, uint32_t flags, void *stream) {
-  if (!A || !BT || !out || M < 1 || N < 1 || K < 1 || shift < 0 || shift > 31)
-    return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_gemm_requant");
-  int dev = 0;
-  CK(cudaGetDevice(&dev));
-  static thread_local anvil_model *scratch[64] = {};
-  if (dev >= 64) return fail(ANVIL_E_BAD_ARG, "device %d out of range", dev);
-  if (!scratch[dev]) {
-    int rc = anvil_model_create(dev, nullptr, 0, &scratch[dev]);
-    if (rc) return rc;
-  }
-  anvil_model *m = scratch[dev];
+// One GEMM + requant on caller-owned device operands (the body of both standalone entry points): launched on
+// m->stream with m->flags as its status words, which are cleared before the launch and read back after it, so a
+// device-side failure (an overflow in checked mode, a device wait that gave up in either mode) is reported by
+// this call whatever the flags. The call synchronises the stream.
+static int standalone_gemm(anvil_model *m, const int8_t *A, const int8_t *BT, int8_t *out, int64_t M, int64_t N,
+                           int64_t K, int32_t mult, int32_t shift, uint32_t flags) {
   Launch L;
   memset(&L.op, 0, sizeof L.op);
   L.op.kind = ANVIL_OP_GEMM;
   L.op.flags = flags & (ANVIL_F_CHECKED | ANVIL_F_SIMT);
   L.op.out_bytes = 1;
+  L.op.op_index = 0;                               // status words record op index + 1: this call is op 0
   L.op.dims[0] = 1; L.op.dims[1] = M; L.op.dims[2] = N; L.op.dims[3] = K;
-  L.op.strides[0] = 0; L.op.strides[1] = 0; L.op.strides[2] = 0; L.op.strides[3] = N;
+  L.op.strides[3] = N;
   L.op.mult = mult;
   L.op.shift = shift;
   for (int s = 0; s < 8; ++s) L.op.off[s] = ANVIL_LOC_NONE;
-  // bypass region resolution: caller-owned device pointers
+  // caller-owned device pointers: no region resolution
   GemmParams &p = L.gp;
   memset(&p, 0, sizeof p);
   p.batch = 1; p.M = M; p.N = N; p.K = K;
@@ -1016,31 +1127,39 @@ extern "C" int anvil_gemm_requant(const int8_t *A, const int8_t *BT, int8_t *out
   p.mult = mult; p.shift = shift; p.out_bytes = 1;
   p.check = (flags & ANVIL_F_CHECKED) ? 1 : 0;
   p.flags = m->flags;
-  L.tc = !(flags & ANVIL_F_SIMT) && K % 16 == 0 && aligned16(A) && aligned16(BT);
-  if (L.tc) {
-    L.bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
-    p.m_tiles = (M + TC_BM - 1) / TC_BM;
-    p.n_tiles = (N + L.bn - 1) / L.bn;
-    p.tiles = p.m_tiles * p.n_tiles;
-    if (int trc = tile_magics(p, -1)) return trc;
-    int rc;
-    if ((rc = make_map_i8(&L.mapA, A, K, M, 1, K, M * K, TC_BM))) return rc;
-    if ((rc = make_map_i8(&L.mapB, BT, K, N, 1, K, N * K, L.bn))) return rc;
-    if ((rc = gemm_out_map(L))) return rc;
+  p.op_index = 0;
+  L.tc = !(flags & ANVIL_F_SIMT) && K % 16 == 0 && aligned16(A) && aligned16(BT) && M <= (1ll << 31) - 256 &&
+         N <= (1ll << 31) - 256;
+  int rc;
+  if (L.tc && (rc = tc_tiles(m, L))) return rc;
+  CK(cudaMemsetAsync(m->flags, 0, FLAG_WORDS * sizeof(uint32_t), m->stream));
+  if ((rc = launch_op(m, L))) return rc;
+  uint32_t h[FLAG_WORDS];
+  CK(cudaMemcpyAsync(h, m->flags, sizeof h, cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  return check_flags(m, h);
+}
+
+extern "C" int anvil_gemm_requant(const int8_t *A, const int8_t *BT, int8_t *out, int64_t M, int64_t N, int64_t K,
+                                  int32_t mult, int32_t shift, uint32_t flags, void *stream) {
+  if (!A || !BT || !out || M < 1 || N < 1 || K < 1 || shift < 0 || shift > 31)
+    return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_gemm_requant");
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  if (dev >= 64) return fail(ANVIL_E_BAD_ARG, "device %d out of range", dev);
+  // one scratch model per device and host thread: its flag words (the only device memory this call uses besides
+  // the caller's operands) are private to the thread, so calls from several threads do not share them
+  static thread_local anvil_model *scratch[64] = {};
+  if (!scratch[dev]) {
+    int rc = anvil_model_create(dev, nullptr, 0, &scratch[dev]);
+    if (rc) return rc;
   }
+  anvil_model *m = scratch[dev];
   cudaStream_t saved = m->stream;
   m->stream = static_cast<cudaStream_t>(stream);
-  if (p.check) CK(cudaMemsetAsync(m->flags, 0, FLAG_WORDS * sizeof(uint32_t), m->stream));
-  int rc = launch_op(m, L);
+  int rc = standalone_gemm(m, A, BT, out, M, N, K, mult, shift, flags);
   m->stream = saved;
-  if (rc) return rc;
-  if (p.check) {
-    uint32_t h[FLAG_WORDS];
-    CK(cudaMemcpyAsync(h, m->flags, sizeof h, cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)));
-    CK(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
-    return check_flags(m, h);
-  }
-  return ANVIL_OK;
+  return rc;
 }
 
 // ------------------------------------------------------------------- standalone GEMM without allocation
@@ -1063,66 +1182,42 @@ extern "C" int anvil_gemm_requant_noalloc(const int8_t *A, const int8_t *BT, int
                 (int)FLAG_WORDS, ANVIL_NOALLOC_SCRATCH_WORDS);
   int dev = 0;
   CK(cudaGetDevice(&dev));
-  if (dev >= 64) return fail(ANVIL_E_BAD_ARG, "device %d out of range", dev);
-  // set-up, once per device, with that device current: the array's device address, the SM count and the kernels'
-  // shared-memory opt-in. None of it allocates.
+  if (dev < 0 || dev >= 64) return fail(ANVIL_E_BAD_ARG, "device %d out of range", dev);
+  // set-up, once per device, with that device current (std::call_once: concurrent first calls on one device wait
+  // for a single set-up): the kernels' shared-memory opt-in and the SM count (device_info), then the array's
+  // device address. None of it allocates.
+  static std::once_flag once[64];
   static uint32_t *scratch_ptr[64] = {};
-  static int sm_count[64] = {};
-  if (!scratch_ptr[dev]) {
+  static int setup_rc[64] = {};
+  static std::string setup_err[64];
+  std::call_once(once[dev], [&]() {
     cudaDeviceProp prop;
-    CK(cudaGetDeviceProperties(&prop, dev));
-    if (prop.major != 10)
-      return fail(ANVIL_E_UNSUPPORTED, "device %d is sm_%d%d; libanvil_cuda is built for sm_100a (B200)", dev,
-                  prop.major, prop.minor);
-    int rc = kernel_attrs(dev);
-    if (rc) return rc;
+    int rc = ANVIL_OK;
     uint32_t *ptr = nullptr;
-    CK(cudaGetSymbolAddress((void **)&ptr, g_noalloc_scratch));
-    sm_count[dev] = prop.multiProcessorCount;
-    scratch_ptr[dev] = ptr;
+    cudaError_t e;
+    if ((e = cudaGetDeviceProperties(&prop, dev)) != cudaSuccess)
+      rc = fail(ANVIL_E_CUDA, "cudaGetDeviceProperties failed: %s", cudaGetErrorString(e));
+    else if (prop.major != 10)
+      rc = fail(ANVIL_E_UNSUPPORTED, "device %d is sm_%d%d; libanvil_cuda is built for sm_100a (B200)", dev,
+                prop.major, prop.minor);
+    else if (!(rc = kernel_attrs(dev)) &&
+             (e = cudaGetSymbolAddress((void **)&ptr, g_noalloc_scratch)) != cudaSuccess)
+      rc = fail(ANVIL_E_CUDA, "cudaGetSymbolAddress of the scratch array failed: %s", cudaGetErrorString(e));
+    setup_rc[dev] = rc;
+    if (rc) setup_err[dev] = g_err;
+    else scratch_ptr[dev] = ptr;
+  });
+  if (setup_rc[dev]) {
+    g_err = setup_err[dev];
+    return setup_rc[dev];
   }
+  DeviceInfo *di = nullptr;
+  int rc = device_info(dev, &di);
+  if (rc) return rc;
   anvil_model m;                                   // a host-side view only: no stream, arena or consts are created
   m.device = dev;
-  m.sms = sm_count[dev];
+  m.sms = di->sms;
   m.stream = static_cast<cudaStream_t>(stream);
-  m.flags = scratch_ptr[dev];
-  Launch L;
-  memset(&L.op, 0, sizeof L.op);
-  L.op.kind = ANVIL_OP_GEMM;
-  L.op.flags = flags & (ANVIL_F_CHECKED | ANVIL_F_SIMT);
-  L.op.out_bytes = 1;
-  L.op.dims[0] = 1; L.op.dims[1] = M; L.op.dims[2] = N; L.op.dims[3] = K;
-  L.op.strides[3] = N;
-  L.op.mult = mult;
-  L.op.shift = shift;
-  for (int s = 0; s < 8; ++s) L.op.off[s] = ANVIL_LOC_NONE;
-  GemmParams &p = L.gp;
-  memset(&p, 0, sizeof p);
-  p.batch = 1; p.M = M; p.N = N; p.K = K;
-  p.o_rstride = N;
-  p.o_cstride = 1;
-  p.A = A; p.BT = BT; p.out = out;
-  p.mult = mult; p.shift = shift; p.out_bytes = 1;
-  p.check = (flags & ANVIL_F_CHECKED) ? 1 : 0;
-  p.flags = m.flags;
-  L.tc = !(flags & ANVIL_F_SIMT) && K % 16 == 0 && aligned16(A) && aligned16(BT);
-  if (L.tc) {
-    L.bn = N <= 64 ? 64 : (N <= 128 ? 128 : 256);
-    p.m_tiles = (M + TC_BM - 1) / TC_BM;
-    p.n_tiles = (N + L.bn - 1) / L.bn;
-    p.tiles = p.m_tiles * p.n_tiles;
-    if (int trc = tile_magics(p, -1)) return trc;
-    int rc;
-    if ((rc = make_map_i8(&L.mapA, A, K, M, 1, K, M * K, TC_BM))) return rc;
-    if ((rc = make_map_i8(&L.mapB, BT, K, N, 1, K, N * K, L.bn))) return rc;
-    if ((rc = gemm_out_map(L))) return rc;
-  }
-  // the array keeps the previous call's words: clear them before this call's kernel can raise any
-  CK(cudaMemsetAsync(m.flags, 0, FLAG_WORDS * sizeof(uint32_t), m.stream));
-  int rc = launch_op(&m, L);
-  if (rc) return rc;
-  uint32_t h[FLAG_WORDS];
-  CK(cudaMemcpyAsync(h, m.flags, sizeof h, cudaMemcpyDeviceToHost, m.stream));
-  CK(cudaStreamSynchronize(m.stream));
-  return check_flags(&m, h);
+  m.flags = scratch_ptr[dev];                      // cleared by standalone_gemm before its kernel can raise any
+  return standalone_gemm(&m, A, BT, out, M, N, K, mult, shift, flags);
 }

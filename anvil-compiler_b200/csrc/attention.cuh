@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         int v[32];
         if (m2_32) {                       // the static int32 proof bounds acc*M2 + 2^(s2-1): 32-bit, clamp in the pack
 #pragma unroll
-          for (int q = 0; q < 32; ++q) v[q] = (acc[q] * (int)p.m2 + (int)rnd2) >> p.s2;
+          for (int q = 0; q < 32; ++q) v[q] = mad_wrap(acc[q], (int)p.m2, (int)rnd2) >> p.s2;
         } else {
 #pragma unroll
           for (int q = 0; q < 32; ++q) v[q] = (int)clampi(((long long)acc[q] * p.m2 + rnd2) >> p.s2, -128, 127);
@@ -370,7 +370,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         // saturating pack.
         int v[32];
 #pragma unroll
-        for (int q = 0; q < 32; ++q) v[q] = (acc[q] * m1 + rnd1) >> p.s1;
+        for (int q = 0; q < 32; ++q) v[q] = mad_wrap(acc[q], m1, rnd1) >> p.s1;
         if (cbase + 32 <= kept) {           // every column of this part is kept: no mask test
 #pragma unroll
           for (int q = 0; q < 32; ++q) mx = max(mx, v[q]);

@@ -26,6 +26,13 @@ __device__ __forceinline__ bool fits_i32(long long v) { return v >= -2147483648L
 
 __device__ __forceinline__ long long round_term(int s) { return s ? (1LL << (s - 1)) : 0LL; }
 
+// a * b + c in 32-bit two's-complement arithmetic (wrap-around, defined for every operand): the unchecked
+// epilogues' form, exact whenever the mathematical value fits int32, which the static int32 proof guarantees for
+// every intermediate it admits. The instruction is the same multiply-add a signed form would compile to.
+__device__ __forceinline__ int mad_wrap(int a, int b, int c) {
+  return (int)((uint32_t)a * (uint32_t)b + (uint32_t)c);
+}
+
 __device__ __forceinline__ int clampi(long long v, int lo, int hi) {
   return (int)(v < lo ? lo : (v > hi ? hi : v));
 }

@@ -51,7 +51,7 @@ template <int OB>
 __device__ __forceinline__ int residual_add(int y, int rv, const GemmParams &p) {
   constexpr int lo = OB == 1 ? -128 : -32768, hi = OB == 1 ? 127 : 32767;
   const int rnd2 = p.shift2 ? 1 << (p.shift2 - 1) : 0;
-  return min(hi, max(lo, (rv * p.ma + y * p.mb + rnd2) >> p.shift2));
+  return min(hi, max(lo, mad_wrap(rv, p.ma, mad_wrap(y, p.mb, rnd2)) >> p.shift2));
 }
 
 // One output element from its int32 accumulator (shared by both kernels).
@@ -534,7 +534,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
           int y[16];
 #pragma unroll
-          for (int q = 0; q < 16; ++q) y[q] = (r[q] * m32 + br[q]) >> sh;
+          for (int q = 0; q < 16; ++q) y[q] = mad_wrap(r[q], m32, br[q]) >> sh;
           if (!RES) {
             if (OB == 1 && lt) {
               // saturate four at a time, bias the bytes by 128 and look each up in this lane's LUT copy

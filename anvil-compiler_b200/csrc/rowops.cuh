@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(256) norm_vec_kernel(const int8_t *__restrict_
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
         const int xc = sext8(ws[q >> 2], q & 3) - mean;
-        int y = ((xc * sext8(ww[q >> 2], q & 3) * r) * m + rnd) >> sh;
+        int y = mad_wrap(mad_wrap(mad_wrap(xc, sext8(ww[q >> 2], q & 3), 0), r, 0), m, rnd) >> sh;
         y += sext8(bb[q >> 2], q & 3);
         y = min(127, max(-128, y));
         o4[q >> 2] |= ((uint32_t)(uint8_t)y) << (8 * (q & 3));
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 
       const int ka = max(0, (32 - __clz(ss) - ln + 1) >> 1);
       k = ka + ((ss >> (2 * ka)) >= n);
     }
-    const int rm = lut[ss >> (2 * k)] * m;
+    const int rm = mad_wrap(lut[ss >> (2 * k)], m, 0);
     const int sh = s + k;
     const int rnd = sh ? 1 << (sh - 1) : 0;
     const uint32_t nm = (uint32_t)(-mean) << 16;
@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 
         asm("prmt.b32 %0, %1, %2, %3;" : "=r"(a) : "r"(q < 4 ? xv[v].x : xv[v].y), "r"(nm),
             "r"((uint32_t)(q & 3) | (uint32_t)((q & 3) | 8) << 4 | 0x7600u));
         const int t = (q & 1) ? __dp2a_hi(a, (int)wp[4 * v + q / 2], 0) : __dp2a_lo(a, (int)wp[4 * v + q / 2], 0);
-        y[q] = ((t * rm + rnd) >> sh) + br[8 * v + q];
+        y[q] = (mad_wrap(t, rm, rnd) >> sh) + br[8 * v + q];
       }
       orow[32 * v] = make_uint2(pack4_sat_s8(y[0], y[1], y[2], y[3]), pack4_sat_s8(y[4], y[5], y[6], y[7]));
     }

@@ -16,7 +16,7 @@ ours (default) prints one JSON line with
                 launch time (CUDA events per launch on the model's stream), against 2 x the measured dense bf16
                 peak (int8 dense rate = 2 x bf16 on B200) or the measured copy bandwidth; traffic from the
                 committed ncu summary; roofline_int8_gemm gives the same for the tcgen05 GEMMs
-  gemm_sweep_c4 config c4 (the int8 GEMM + requant sweep) through anvil_gemm_requant, sampled rows bit-exact
+  gemm_sweep_c4 config c4 (the int8 GEMM + requant sweep) as one-op graphs, sampled rows bit-exact
   cpu_baseline  the oracle port (numpy restatement of anvil.interp) on rank 0 at N = 1, one bounded sample
   clocks        nvidia-smi samples taken during the timed region
 --impl reference times that CPU oracle alone (rank 0), with a process pool over all host cores.
@@ -288,7 +288,7 @@ def run_ours(args):
     cm, gen = W.compile_config(cfg, params=CudaParams(devices=(local,)))
     prog = cm.program(batch)
     dm = cm._device_model(local)
-    dm.prepare(prog.ops, prog.plan.arena, key=(batch, "outputs"))
+    dm.prepare(prog.ops, prog.plan.arena, key=(batch, "outputs", False))
     # inputs: quantized once on the host, in pinned memory (the e2e path copies them in every step)
     x = gen(batch)
     xq = cm.quantize_input(x) if cm.meta[cm.inputs[0]][0] is not None else x
@@ -304,16 +304,16 @@ def run_ours(args):
         print(json.dumps({"profile_runs": args.profile_runs, "launches_per_run": len(prog.ops), "batch": batch}))
         dm.close()
         return 0
-    # correctness gate: one sequence of the device result against the oracle (rank 0, before timing)
-    if rank == 0 and not args.skip_check:
+    # correctness gate on the very program the timed loop replays: one CUDA-graph replay of the prepared batch,
+    # then sampled sequences of its outputs (first, middle, last) against the oracle; the same sequences are checked
+    # again after the timed replays
+    sample = sorted({0, batch // 2, batch - 1})
+    want = None
+    if not args.skip_check:
         from oracle import interp
-        res = cm.run(xin[:1], "cuda", quantized=True)
-        want = interp.run(cm.module, {cm.inputs[0]: np.asarray(xq[:1])}, cm.consts, batch=True)
-        for s in cm.outputs:
-            if not np.array_equal(res.ints[s], want.values[s]):
-                raise SystemExit(f"bench: {s} differs from the oracle")
-        dm.prepare(prog.ops, prog.plan.arena, key=(batch, "outputs"))
-        dm.write(off, xin)
+        want = interp.run(cm.module, {cm.inputs[0]: np.asarray(xq[sample])}, cm.consts, batch=True)
+        dm.run_device(1, use_graph=True)
+        _gate(cm, prog, dm, sample, want, "before the timed replays")
     tokens = batch * c.seq
     # warm-up (also captures the CUDA graph)
     dm.run_device(max(1, args.warmup), use_graph=True)
@@ -325,6 +325,8 @@ def run_ours(args):
         ms = dm.run_device(args.steps, use_graph=True)
         torch.cuda.synchronize()
         _barrier(dist, local)
+    if want is not None:
+        _gate(cm, prog, dm, sample, want, "after the timed replays")
     ms = _max_over_ranks(dist, ms, f"cuda:{local}")
     ms_step = ms / args.steps
     value = ws * tokens / (ms_step / 1000.0)
@@ -389,14 +391,28 @@ def run_ours(args):
     return 0
 
 
+def _gate(cm, prog, dm, sample, want, when):
+    """The graph outputs of sequences `sample`, read from the device arena of the prepared program, must equal the
+    oracle's (`want`, computed on those sequences); exits non-zero otherwise."""
+    from anvil.driver import _apply_view
+    for sym, v in prog.outputs:
+        if sym is None or v.const:
+            continue
+        buf = dm.read(prog.plan.addresses[v.root], np.empty(prog.buffers[v.root], dtype=np.uint8))
+        got = _apply_view(buf, v)[sample]
+        if not np.array_equal(got, want.values[sym]):
+            bad = np.argwhere(got != want.values[sym])
+            raise SystemExit(f"bench: {sym} of sequences {sample} differs from the oracle {when} "
+                             f"({len(bad)} values, first at {bad[0].tolist()})")
+
+
 # What each family's ncu capture shows it waits on (the summaries under profiles/ give the figures).
 LIMITERS = {
     "attention": "integer issue of the 16 softmax warps (about 23 instructions per kept score element across the "
-                 "requant / row-sum / probability passes; ALU pipe the busiest), not the tensor pipe or DRAM: "
-                 "profiles/attn_kernel_c3_b64.md",
+                 "requant / row-sum / probability passes; ALU pipe the busiest), not the tensor pipe or DRAM",
     "gemm": "K = 3072: the tensor pipe (88 % active); K = 768: the epilogue warps draining each accumulator "
-            "(requant, bias, LUT or residual, pack, TMA store): profiles/qgemm_tc_c3_b64.md",
-    "norm": "instruction issue and row-load latency of one warp per 768-byte row: profiles/norm_row_c3_b64.md",
+            "(requant, bias, LUT or residual, pack, TMA store)",
+    "norm": "instruction issue and row-load latency of one warp per 768-byte row",
 }
 
 
@@ -439,40 +455,44 @@ def _rooflines(prog, kus, hbm, bf16, src, C, i8peak=None):
     return out
 
 
-def gemm_sweep(peak_tops, reps=5):
-    """Config c4: int8 GEMM + requant at M in {1024, 8192, 65536}, K = N in {768, 3072, 4096} through
-    anvil_gemm_requant on device-resident operands; TOP/s from CUDA events, and 8 sampled rows per shape checked
-    bit-exact against the oracle."""
-    import torch
+def gemm_sweep(peak_tops, reps=20):
+    """Config c4: int8 GEMM + requant at M in {1024, 8192, 65536}, K = N in {768, 3072, 4096}, each shape as a
+    one-op graph (qlinear: A an input, B a constant) through anvil.compile on the cuda target: the same tcgen05 GEMM
+    kernels and tile choice as anvil_gemm_requant, timed as `reps` CUDA-graph replays with CUDA events on the
+    model's stream (the standalone entry point synchronises on its status words every call, so it is not what a
+    kernel timing should wrap); 8 sampled rows per shape checked bit-exact against the oracle. Operands of the
+    smaller shapes stay in L2 across replays."""
+    import warnings
     from anvil import workloads as W
-    from anvil.runtime import cuda as C
+    from anvil.driver import CudaParams, compile as anvil_compile
+    from anvil.ir import GraphBuilder
     from oracle import semantics as osem
     res = []
     for m, k, n in W.GEMM_SWEEP:
         a, b, mult, s = W.gemm_case(m, k, n)
-        ta = torch.from_numpy(a).cuda()
-        tbt = torch.from_numpy(np.ascontiguousarray(b.T)).cuda()
-        out = torch.empty((m, n), dtype=torch.int8, device="cuda")
-        st = torch.cuda.current_stream()
-        call = lambda: C.gemm_requant(ta.data_ptr(), tbt.data_ptr(), out.data_ptr(), m, n, k, mult, s, 0,  # noqa
-                                      st.cuda_stream)
-        for _ in range(3):
-            call()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        e0.record(st)
-        for _ in range(reps):
-            call()
-        e1.record(st)
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1000 / reps
+        g = GraphBuilder("c4")
+        x = g.input("a", [m, k], "i8")
+        g.output(g.qlinear("out", x, g.const("b", [k, n], "i8"), int(mult), int(s)))
+        with warnings.catch_warnings():          # the data is U[-127, 127]: no intermediate can overflow
+            warnings.simplefilter("ignore", RuntimeWarning)
+            cm = anvil_compile(g.module(), consts={"b": b.astype(np.int64)}, prove=False,
+                               params=CudaParams(checked=False, gemm="tc"))
+        prog = cm.program(1)
+        dm = cm._device_model(0)
+        dm.prepare(prog.ops, prog.plan.arena, key=(1, "outputs", False))
+        dm.write(prog.inputs["a"][0], a)
+        dm.run_device(3, use_graph=True)
+        us = dm.run_device(reps, use_graph=True) * 1000 / reps
+        (sym, v), = [(sy, vw) for sy, vw in prog.outputs if sy is not None]
+        out = dm.read(prog.plan.addresses[v.root], np.empty((m, n), dtype=np.int8))
         rows = np.random.default_rng(m + k).choice(m, 8, replace=False)
         want = osem.requant(osem.matmul_i8(a[rows].astype(np.int64), b.astype(np.int64)), mult, s)
-        exact = bool(np.array_equal(out.cpu().numpy()[rows].astype(np.int64), want))
+        exact = bool(np.array_equal(out[rows].astype(np.int64), want))
         tops = 2 * m * n * k / (us * 1e-6) / 1e12
         res.append({"M": m, "K": k, "N": n, "us": round(us, 2), "tops": round(tops, 1),
-                    "frac": round(tops / peak_tops, 4), "rows_exact": exact})
-        del ta, tbt, out
+                    "frac": round(tops / peak_tops, 4), "rows_exact": exact, "kernel": prog.devops[0].label,
+                    "l2": "operands larger than L2" if m * k + k * n > 126e6 else "operands fit L2 (warm)"})
+        dm.close()
     return res
 
 

@@ -171,6 +171,17 @@ ANVIL_API int anvil_model_selftest_timeout(anvil_model *m, uint64_t wait_ns);
 ANVIL_API int anvil_model_read(anvil_model *m, uint64_t offset, void *host, uint64_t bytes);
 ANVIL_API int anvil_model_write(anvil_model *m, uint64_t offset, const void *host, uint64_t bytes);
 
+/* Read raw bytes of the const region, for the stray-write check of a guarded run: a run must leave every const
+ * byte as uploaded (the reference's RunOutput.stray_writes, anvil/driver.py:66-71, and JobPlan.stray_writes,
+ * anvil/codegen/__init__.py:150-168, check consts and every word outside the plan's buffers). */
+ANVIL_API int anvil_model_read_const(anvil_model *m, uint64_t offset, void *host, uint64_t bytes);
+
+/* The launch shape the library chose for prepared op `op` (for summaries and tests): info[0..3] =
+ * GEMM: {BN (64 | 128 | 256; 0 for the CUDA-core kernel), CTAs per tile (1, or 2 for CTA-pair 256-row tiles), tiles,
+ * CTAs launched}; ATTENTION: {hd, 0, (batch, head, 128-query) work items, CTAs launched}; other kinds: zeros.
+ * The reference's counterpart is the per-kernel schedule its summary prints (anvil/driver.py:324-327). */
+ANVIL_API int anvil_model_describe(anvil_model *m, int op, int64_t *info);
+
 /* Device pointer of the arena and of the const region (for callers that bring their own device buffers). */
 ANVIL_API int anvil_model_arena(anvil_model *m, uint64_t *arena_ptr, uint64_t *const_ptr);
 
@@ -180,7 +191,10 @@ ANVIL_API void anvil_model_free(anvil_model *m);
  * out[M, N] = clamp((A[M, K] @ B[K, N] * mult + 2^(shift-1)) >> shift) as int8, with BT = B transposed
  * ([N, K] row-major, K contiguous). Runs on `stream` (cudaStream_t, NULL = legacy default). `flags` takes
  * ANVIL_F_CHECKED / ANVIL_F_SIMT. Bit-exact to requant(matmul_i8(A, B), mult, shift) (anvil/semantics.py:95-103)
- * whenever that raises nothing. */
+ * whenever that raises nothing. The tile shape (64, 128 or 256 columns, single-CTA or CTA-pair 256-row tiles) is
+ * chosen by how evenly the tiles fill the SMs. The call synchronises `stream` and reports the kernel's device
+ * status in every mode: ANVIL_E_OVERFLOW (checked mode) or ANVIL_E_TIMEOUT (a bounded device wait gave up). Each
+ * host thread has its own status words, so calls from several threads do not share them. */
 ANVIL_API int anvil_gemm_requant(const int8_t *A, const int8_t *BT, int8_t *out, int64_t M, int64_t N, int64_t K,
                        int32_t mult, int32_t shift, uint32_t flags, void *stream);
 
@@ -191,7 +205,8 @@ ANVIL_API int anvil_gemm_requant(const int8_t *A, const int8_t *BT, int8_t *out,
  * static array of 16 32-bit words (64 bytes) that every GPU loading the library holds until the process exits; the
  * GEMM uses 4 of them as its overflow / index / timeout status words and the call fails with ANVIL_E_BAD_ARG if it
  * ever needed more than the array holds. The first call on a device does a one-time set-up there (it looks up the
- * array's device address and the kernels' shared-memory limits), so make that first call before any stream capture.
+ * array's device address and the kernels' shared-memory limits), so make that first call before any stream capture;
+ * first calls from several host threads on one device are safe (one set-up runs, the others wait for it).
  * All calls share the array: it is cleared at the start of each call, and calls that overlap on the GPU (other
  * streams, other host threads) race on it. The call synchronises `stream` before it returns. */
 ANVIL_API int anvil_gemm_requant_noalloc(const int8_t *A, const int8_t *BT, int8_t *out, int64_t M, int64_t N,

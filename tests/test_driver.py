@@ -81,3 +81,19 @@ def test_summary_lists_every_launch():
     m, c = _graph()
     text = anvil.compile(m, consts=c).summary(batch=2)
     assert "gemm" in text and "footprint" in text and "checked: False" in text
+
+
+def test_summary_gives_the_roofline_fraction_of_each_timed_launch():
+    """With measured microseconds (RunOutput.cycles of a timing run) every launch shows its achieved rate and the
+    fraction of the roofline bounding it: ops against the int8 tensor peak, bytes against HBM bandwidth."""
+    m, c = _graph()
+    cm = anvil.compile(m, consts=c)
+    labels = [d.label for d in cm.program(2).devops]
+    text = cm.summary(batch=2, kernel_us={lab: 10.0 for lab in labels}, peaks={"int8_tops": 1000.0, "hbm_gbs": 5000.0})
+    rows = text.splitlines()[:len(labels)]
+    assert all(" us " in r and "% of " in r for r in rows)
+    d = cm.program(2).devops[0]
+    if "ops" in d.work:
+        want = d.work["ops"] / 10e-6 / 1e12 / 1000.0
+        assert f"{want:6.1%}" in rows[0]
+    assert "1000.0 int8 TOP/s, 5000.0 GB/s" in text

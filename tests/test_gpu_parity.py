@@ -232,7 +232,7 @@ def test_device_replays_keep_the_inputs():
     want = interp.run(cm.module, {cm.inputs[0]: ids}, cm.consts, batch=True)
     prog = cm.program(4)
     dm = cm._device_model(0)
-    dm.prepare(prog.ops, prog.plan.arena, key=(4, "outputs"))
+    dm.prepare(prog.ops, prog.plan.arena, key=(4, "outputs", False))
     dm.write(prog.inputs[cm.inputs[0]][0], np.ascontiguousarray(ids, dtype=np.int32))
     dm.run_device(3, use_graph=True)
     for sym, v in prog.outputs:

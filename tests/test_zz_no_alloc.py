@@ -77,3 +77,28 @@ def test_noalloc_rejects_bad_arguments():
     f = _noalloc()
     with pytest.raises(ValueError):
         C.check(f(None, None, None, 0, 1, 1, 1, 0, 0, None), "anvil_gemm_requant_noalloc")
+
+
+@pytest.mark.parametrize("flags", [0, C.F_CHECKED])
+def test_both_entry_points_report_the_same_status(flags):
+    """On operands whose products leave int32 both entry points return the same status for the same flags: the
+    overflow (OverflowError) when checked, success when unchecked; and they write the same bytes."""
+    import torch
+    f = _noalloc()
+    m, n, k = 64, 64, 64
+    stream = torch.cuda.current_stream().cuda_stream
+    a = torch.full((m, k), 127, dtype=torch.int8, device="cuda")
+    bt = torch.full((n, k), 127, dtype=torch.int8, device="cuda")
+    outs, codes = [], []
+    for call in ("alloc", "noalloc"):
+        out = torch.zeros((m, n), dtype=torch.int8, device="cuda")
+        if call == "alloc":
+            rc = C.load_library().anvil_gemm_requant(a.data_ptr(), bt.data_ptr(), out.data_ptr(), m, n, k, 1 << 20, 4,
+                                                     flags, stream or None)
+        else:
+            rc = f(a.data_ptr(), bt.data_ptr(), out.data_ptr(), m, n, k, 1 << 20, 4, flags, stream or None)
+        torch.cuda.synchronize()
+        outs.append(out.cpu())
+        codes.append(rc)
+    assert codes[0] == codes[1] == (-5 if flags else 0)
+    assert torch.equal(outs[0], outs[1])
