@@ -244,8 +244,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       // S = Q K_j^T for the next K tile into the next S buffer (the tile's Q is resident)
       auto issue_s = [&]() -> bool {
         const int sb = gs % Cfg::NSB, st = gk % Cfg::KS;
-        if (!mbar_wait(&sempty[sb], ((gs / Cfg::NSB) & 1) ^ 1, abort, p.flags, p.op_index)) return false;
-        if (!mbar_wait(&kfull[st], (gk / Cfg::KS) & 1, abort, p.flags, p.op_index)) return false;
+        if (!mbar_wait_idle(&sempty[sb], ((gs / Cfg::NSB) & 1) ^ 1, abort, p.flags, p.op_index)) return false;
+        if (!mbar_wait_idle(&kfull[st], (gk / Cfg::KS) & 1, abort, p.flags, p.op_index)) return false;
         tc_fence_after();
         const uint32_t sk = smem_u32(smem + Cfg::OFF_K + st * Cfg::T_BYTES);
 #pragma unroll
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       int t = attn_item(0, ntiles);
       if (t >= 0) {                     // the first tile's first NSB score MMAs
         const AttnTile w = attn_tile(p, t);
-        ok = mbar_wait(qfull, 0, abort, p.flags, p.op_index);
+        ok = mbar_wait_idle(qfull, 0, abort, p.flags, p.op_index);
         tc_fence_after();
         for (int j = 0; ok && j < min(Cfg::NSB, w.nkv); ++j) ok = issue_s();
       }
@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           const int st = gv % Cfg::VS;
           if (!mbar_wait_idle(&pslab[j], (pph >> j) & 1u, abort, p.flags, p.op_index)) { ok = false; break; }
           pph ^= 1u << j;
-          if (!mbar_wait(&vfull[st], (gv / Cfg::VS) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
+          if (!mbar_wait_idle(&vfull[st], (gv / Cfg::VS) & 1, abort, p.flags, p.op_index)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sp = smem_u32(pbuf + j * Cfg::P_SLAB);
           const uint32_t sv = smem_u32(smem + Cfg::OFF_V + st * Cfg::T_BYTES);
@@ -309,6 +309,11 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     const int r = lane_base + lane;
     const int m1 = (int)p.m1;
     const int rnd1 = (int)round_term(p.s1);
+    // With s1 >= 1 and m1 < 2^(s1-1), M1w = m1 * 2^(32-s1) fits int32 and the high word of the 64-bit
+    // acc * M1w + 2^31 is (acc * m1 + 2^(s1-1)) >> s1 exactly: one wide multiply-add instead of a multiply-add and
+    // a shift (and off the ALU pipe)
+    const bool wide1 = p.s1 >= 1 && p.m1 >= 0 && p.m1 < (1ll << (p.s1 - 1));
+    const int m1w = wide1 ? (int)((uint32_t)p.m1 << (32 - p.s1)) : 0;
     int32_t *red_max = reinterpret_cast<int32_t *>(smem + Cfg::OFF_RED);   // [4][128] partial row max
     int32_t *red_sum = red_max + 512;                                          // [4][128] partial row sum
     const int lcopy = lane % Cfg::LUT_COPIES;
@@ -350,10 +355,15 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     AttnTile prev;
     int k = 0;
     bool stopped = false;
+    // this thread's two 16-byte chunks of every P slab (the swizzle depends on the row only)
+    const int off0 = pslab_off(r, 2 * part), off1 = pslab_off(r, 2 * part + 1);
     for (int t; (t = attn_item(k, ntiles)) >= 0; ++k) {
       const AttnTile w = attn_tile(p, t);
       const int row = w.q0 + r;
       const int kept = p.causal ? min(row + 1, p.T2) : p.T2;
+      // Every pass classifies this thread's 32 columns of slab j for the warp as a whole (votes, so the branches
+      // are warp-uniform): all kept for every row of the warp (no mask), none kept (nothing to read), or the
+      // causal diagonal / the ragged end of T2 (a per-lane mask, by selects).
       int mx = -128;
       bool ok = true;
       for (int j = 0; j < w.nkv; ++j, ++gs) {
@@ -363,34 +373,31 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         tc_fence_after();
         int32_t acc[32];
         tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(sb * 128 + part * 32), acc);
-        uint32_t wq[8];
-        const int cbase = j * 128 + part * 32;
+        const int cb = j * 128 + part * 32;
         // the static int32 proof holds on this path: acc*M1 + 2^(s1-1) fits int32. The row max is taken over the
         // unclamped values (clamping is monotone, so max of clamped = clamp of max) and the clamp happens in the
         // saturating pack.
         int v[32];
 #pragma unroll
-        for (int q = 0; q < 32; ++q) v[q] = mad_wrap(acc[q], m1, rnd1) >> p.s1;
-        if (cbase + 32 <= kept) {           // every column of this part is kept: no mask test
+        for (int q = 0; q < 32; ++q)
+          v[q] = wide1 ? (int)(((long long)acc[q] * m1w + 0x80000000ll) >> 32) : mad_wrap(acc[q], m1, rnd1) >> p.s1;
+        if (__all_sync(0xffffffffu, cb + 32 <= kept)) {
 #pragma unroll
           for (int q = 0; q < 32; ++q) mx = max(mx, v[q]);
         } else {
 #pragma unroll
-          for (int q = 0; q < 32; ++q)
-            if (cbase + q < kept) mx = max(mx, v[q]);
+          for (int q = 0; q < 32; ++q) mx = max(mx, cb + q < kept ? v[q] : -128);
         }
-        // the slab holds each score biased by 128 (x + 128 as an unsigned byte), so both passes below read it
-        // with one zero-extending byte extract; pass B overwrites it with the probabilities
+        uint32_t wq[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-          wq[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]) ^ 0x80808080u;
+        for (int q = 0; q < 8; ++q) wq[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         // P slab j still feeds the previous tile's P V MMA until pfree[j] completes
         ok = __all_sync(0xffffffffu, mbar_wait(&pfree[j], ((fph >> j) & 1u) ^ 1u, abort, p.flags, p.op_index));
         fph ^= 1u << j;
         if (!ok) break;
         uint8_t *slab = pbuf + j * Cfg::P_SLAB;
-        *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part)) = make_uint4(wq[0], wq[1], wq[2], wq[3]);
-        *reinterpret_cast<uint4 *>(slab + pslab_off(r, 2 * part + 1)) = make_uint4(wq[4], wq[5], wq[6], wq[7]);
+        *reinterpret_cast<uint4 *>(slab + off0) = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+        *reinterpret_cast<uint4 *>(slab + off1) = make_uint4(wq[4], wq[5], wq[6], wq[7]);
         tc_fence_before();
         mbar_arrive(&sempty[sb]);
       }
@@ -412,32 +419,30 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           : "memory");
       if (stop) { stopped = true; break; }
       mx = max(max(red_max[r], red_max[128 + r]), max(red_max[256 + r], red_max[384 + r]));
-      // a kept score x <= mx is stored as u = x + 128, and lut[x - mx + 255] = lut[u + 127 - mx]: lutc[u * COPIES]
-      // is that entry in this lane's copy (index 0..255 for every kept u)
-      const int32_t *lutc = lut + (127 - mx) * Cfg::LUT_COPIES + lcopy;
+      // a kept score x <= mx (a signed byte of the slab) has lut[x - mx + 255] at lutc[x * COPIES] in this lane's
+      // copy; a masked column's byte may exceed mx and is clamped to it first, so every index is in [0, 255]
+      const int32_t *lutc = lut + (255 - mx) * Cfg::LUT_COPIES + lcopy;
       // pass A: partial S = sum over this part's kept columns of lut[x - max + 255]
       int tot0 = 0, tot1 = 0;
       for (int j = 0; j < w.nkv && ok; ++j) {
+        const int cb = j * 128 + part * 32;
+        if (__all_sync(0xffffffffu, cb >= kept)) continue;
         const uint8_t *slab = pbuf + j * Cfg::P_SLAB;
+        const uint4 a4 = *reinterpret_cast<const uint4 *>(slab + off0);
+        const uint4 b4 = *reinterpret_cast<const uint4 *>(slab + off1);
+        const uint32_t wv[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
+        if (__all_sync(0xffffffffu, cb + 32 <= kept)) {
+          // two independent three-input adds per word (each folds two entries into one accumulator)
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int c0 = j * 128 + part * 32 + hh * 16;
-          if (c0 < kept) {
-            const uint4 v4 = *reinterpret_cast<const uint4 *>(slab + pslab_off(r, 2 * part + hh));
-            const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
-            if (c0 + 16 <= kept) {
-              // two independent three-input adds per word (each folds two entries into one accumulator)
+          for (int q = 0; q < 8; ++q) {
+            tot0 += lutc[sbyte_prmt(wv[q], 0) * Cfg::LUT_COPIES] + lutc[sbyte_prmt(wv[q], 1) * Cfg::LUT_COPIES];
+            tot1 += lutc[sbyte_prmt(wv[q], 2) * Cfg::LUT_COPIES] + lutc[sbyte_prmt(wv[q], 3) * Cfg::LUT_COPIES];
+          }
+        } else {
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                tot0 += lutc[ubyte(wv[q], 0) * Cfg::LUT_COPIES] + lutc[ubyte(wv[q], 1) * Cfg::LUT_COPIES];
-                tot1 += lutc[ubyte(wv[q], 2) * Cfg::LUT_COPIES] + lutc[ubyte(wv[q], 3) * Cfg::LUT_COPIES];
-              }
-            } else {
-#pragma unroll
-              for (int q = 0; q < 16; ++q) {
-                if (c0 + q < kept) tot0 += lutc[ubyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES];
-              }
-            }
+          for (int q = 0; q < 32; ++q) {
+            const int e = lutc[min(sbyte_prmt(wv[q >> 2], q & 3), mx) * Cfg::LUT_COPIES];
+            tot0 += cb + q < kept ? e : 0;
           }
         }
       }
@@ -458,35 +463,32 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       const unsigned half2 = S > 1 ? (unsigned)(tot >> 1) : 2u * (unsigned)(tot >> 1);
       for (int j = 0; j < w.nkv && ok; ++j) {
         uint8_t *slab = pbuf + j * Cfg::P_SLAB;
+        const int cb = j * 128 + part * 32;
+        uint32_t ov[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (!__all_sync(0xffffffffu, cb >= kept)) {
+          const uint4 a4 = *reinterpret_cast<const uint4 *>(slab + off0);
+          const uint4 b4 = *reinterpret_cast<const uint4 *>(slab + off1);
+          const uint32_t wv[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
+          int pv[32];
+          if (__all_sync(0xffffffffu, cb + 32 <= kept)) {
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int c0 = j * 128 + part * 32 + hh * 16;
-          const int off = pslab_off(r, 2 * part + hh);
-          uint4 v4 = *reinterpret_cast<const uint4 *>(slab + off);
-          const uint32_t wv[4] = {v4.x, v4.y, v4.z, v4.w};
-          uint32_t ov[4] = {0, 0, 0, 0};
-          if (c0 + 16 <= kept) {
-            int pv[16];
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              const unsigned num = (unsigned)lutc[ubyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES] * one2 + half2;
+            for (int q = 0; q < 32; ++q) {
+              const unsigned num = (unsigned)lutc[sbyte_prmt(wv[q >> 2], q & 3) * Cfg::LUT_COPIES] * one2 + half2;
               pv[q] = (int)(__umulhi(num, magic) >> msh);
             }
+          } else {
 #pragma unroll
-            for (int q = 0; q < 4; ++q) ov[q] = pack4_sat_s8(pv[4 * q], pv[4 * q + 1], pv[4 * q + 2], pv[4 * q + 3]);
-          } else if (c0 < kept) {
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              unsigned pq = 0;
-              if (c0 + q < kept) {
-                const unsigned num = (unsigned)lutc[ubyte(wv[q >> 2], q & 3) * Cfg::LUT_COPIES] * one2 + half2;
-                pq = __umulhi(num, magic) >> msh;
-              }
-              ov[q >> 2] |= (pq & 0xffu) << (8 * (q & 3));
+            for (int q = 0; q < 32; ++q) {
+              const int x = min(sbyte_prmt(wv[q >> 2], q & 3), mx);
+              const unsigned num = (unsigned)lutc[x * Cfg::LUT_COPIES] * one2 + half2;
+              pv[q] = cb + q < kept ? (int)(__umulhi(num, magic) >> msh) : 0;
             }
           }
-          *reinterpret_cast<uint4 *>(slab + off) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) ov[q] = pack4_sat_s8(pv[4 * q], pv[4 * q + 1], pv[4 * q + 2], pv[4 * q + 3]);
         }
+        *reinterpret_cast<uint4 *>(slab + off0) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+        *reinterpret_cast<uint4 *>(slab + off1) = make_uint4(ov[4], ov[5], ov[6], ov[7]);
         fence_proxy_async();                // this thread's part of slab j is final: the P V MMA may read it
         mbar_arrive(&pslab[j]);
       }

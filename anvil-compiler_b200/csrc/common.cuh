@@ -72,6 +72,15 @@ __device__ __forceinline__ uint32_t pack4_sat_s8(int a0, int a1, int a2, int a3)
 // Signed byte q (0..3) of w, sign-extended: always in [-128, 127].
 __device__ __forceinline__ int sbyte(uint32_t w, int q) { return (int)(int8_t)(w >> (8 * q)); }
 
+// Sign-extended byte q (0..3) of w in one byte permute: prmt's default mode replicates the sign bit of the
+// selected byte when the selector nibble's msb is set, so bytes 1-3 of the result copy the sign of byte q.
+__device__ __forceinline__ int sbyte_prmt(uint32_t w, int q) {
+  int r;
+  const uint32_t sel = (uint32_t)q | ((uint32_t)(q | 8) * 0x1110u);
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(sel));
+  return r;
+}
+
 // Unsigned byte q (0..3) of w, zero-extended (one byte permute): always in [0, 255].
 __device__ __forceinline__ uint32_t ubyte(uint32_t w, int q) { return __byte_perm(w, 0u, 0x4440u | (uint32_t)q); }
 

@@ -178,7 +178,7 @@ struct TcCfg {
   static constexpr int BAR_OFF = STG_OFF + STG_BYTES;
   static constexpr int MISC_OFF = BAR_OFF + (2 * STAGES + 4) * 8;
   static constexpr int BST_OFF = MISC_OFF + 16;
-  static constexpr int SMEM_BYTES = BST_OFF + TC_EPI_WARPS * 64 + 1024;   // + 1 KB slack to align the ring
+  static constexpr int SMEM_BYTES = BST_OFF + TC_EPI_WARPS * 128 + 1024;  // + 1 KB slack to align the ring
 };
 
 // Load 32 consecutive int8 / int16 values of a row (vector loads when the chunk is whole and aligned).
@@ -443,12 +443,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr int NSC = Cfg::NSC;
     const int lane_base = 32 * (warp & 3);
     const int cq = (warp - 2) >> 2;
-    int32_t *bslot = bst + (warp - 2) * 16;
+    int32_t *bslot = bst + (warp - 2) * 32;                   // 16 columns x (int32 or 64-bit) staged bias
     int acc = 0;
     uint32_t aphase = 0;
     constexpr int lo = OB == 1 ? -128 : -32768, hi = OB == 1 ? 127 : 32767;
     const int32_t *lt = p.lut ? lut_r + lane : nullptr;       // this lane's copy: lt[32 e] = lut[e]
     const int m32 = (int)p.mult, sh = p.shift, rnd = sh ? 1 << (sh - 1) : 0;
+    // With s >= 1 and M < 2^(s-1), Mw = M * 2^(32-s) fits int32 and the high word of the 64-bit
+    // acc * Mw + (bias*M + 2^(s-1)) * 2^(32-s) is (acc * M + bias*M + 2^(s-1)) >> s exactly: one wide multiply-add
+    // per output instead of a multiply-add and a shift (the shift being on the busier ALU pipe)
+    const bool wide = !p.check && sh >= 1 && p.mult >= 0 && p.mult < (1ll << (sh - 1));
+    const int mw = wide ? (int)((uint32_t)p.mult << (32 - sh)) : 0;
     // fused residual with i8 y and i8 residual: both enter biased by 128 (u = x + 128, one byte extract each),
     // and -128 (Ma + Mb) folds into the rounding constant; the sum is formed mod 2^32 and is exact because the
     // static int32 proof bounds the true value
@@ -518,23 +523,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         } else {
           // the static int32 proof holds: (acc [+ bias]) * M + 2^(s-1) fits int32, so 32-bit wrap-free math is
           // exact; a bias arrives pre-folded as bias*M + 2^(s-1) (ANVIL_F_BIAS_RND)
-          int br[16];
-          if (p.bias) {
-            __syncwarp();
-            if (lane < 16) bslot[lane] = bcur;
-            __syncwarp();
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int4 b4 = reinterpret_cast<const int4 *>(bslot)[q];
-              br[4 * q] = b4.x; br[4 * q + 1] = b4.y; br[4 * q + 2] = b4.z; br[4 * q + 3] = b4.w;
-            }
-          } else {
-#pragma unroll
-            for (int q = 0; q < 16; ++q) br[q] = rnd;
-          }
           int y[16];
+          if (wide) {
+            long long ad[16];                           // (bias*M + 2^(s-1)) * 2^(32-s), or 2^31 without a bias
+            if (p.bias) {
+              __syncwarp();
+              if (lane < 16) reinterpret_cast<long long *>(bslot)[lane] = (long long)bcur << (32 - sh);
+              __syncwarp();
 #pragma unroll
-          for (int q = 0; q < 16; ++q) y[q] = mad_wrap(r[q], m32, br[q]) >> sh;
+              for (int q = 0; q < 8; ++q) {
+                const longlong2 b2 = reinterpret_cast<const longlong2 *>(bslot)[q];
+                ad[2 * q] = b2.x;
+                ad[2 * q + 1] = b2.y;
+              }
+            } else {
+#pragma unroll
+              for (int q = 0; q < 16; ++q) ad[q] = 0x80000000ll;
+            }
+#pragma unroll
+            for (int q = 0; q < 16; ++q) y[q] = (int)(((long long)r[q] * mw + ad[q]) >> 32);
+          } else {
+            int br[16];
+            if (p.bias) {
+              __syncwarp();
+              if (lane < 16) bslot[lane] = bcur;
+              __syncwarp();
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int4 b4 = reinterpret_cast<const int4 *>(bslot)[q];
+                br[4 * q] = b4.x; br[4 * q + 1] = b4.y; br[4 * q + 2] = b4.z; br[4 * q + 3] = b4.w;
+              }
+            } else {
+#pragma unroll
+              for (int q = 0; q < 16; ++q) br[q] = rnd;
+            }
+#pragma unroll
+            for (int q = 0; q < 16; ++q) y[q] = mad_wrap(r[q], m32, br[q]) >> sh;
+          }
           if (!RES) {
             if (OB == 1 && lt) {
               // saturate four at a time, bias the bytes by 128 and look each up in this lane's LUT copy

@@ -262,14 +262,6 @@ __global__ void __launch_bounds__(256) norm_vec_kernel(const int8_t *__restrict_
   }
 }
 
-// Sign-extended byte q (0..3) of w in one byte permute: prmt's default mode replicates the sign bit of the
-// selected byte when the selector nibble's msb is set, so bytes 1-3 of the result copy the sign of byte q.
-__device__ __forceinline__ int sbyte_prmt(uint32_t w, int q) {
-  int r;
-  const uint32_t sel = (uint32_t)q | ((uint32_t)(q | 8) * 0x1110u);
-  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(sel));
-  return r;
-}
 
 // norm_vec for rows of d = 256 * NV8 int8 values (unchecked, static int32 proof). One warp per row, every lane
 // NV8 8-byte vectors (lane + 32 v); the weights (as dp2a byte pairs) and the bias held in registers once per
@@ -350,6 +342,11 @@ __global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 
     const int sh = s + k;
     const int rnd = sh ? 1 << (sh - 1) : 0;
     const uint32_t nm = (uint32_t)(-mean) << 16;
+    // With 1 <= sh <= 32 and 0 <= rm < 2^(sh-1), RM = rm * 2^(32-sh) fits int32 and the high word of the 64-bit
+    // t * RM + bias * 2^32 + 2^31 is ((t * rm + 2^(sh-1)) >> sh) + bias exactly: one wide multiply-add does the
+    // rescale, the rounding shift and the bias. Other rows take the 32-bit multiply-add, shift and add.
+    const bool wide = sh >= 1 && sh <= 32 && rm >= 0 && (sh == 32 || rm < (1 << (sh - 1)));
+    const int RM = wide ? (int)((uint32_t)rm << (32 - sh)) : 0;
 #pragma unroll
     for (int v = 0; v < NV8; ++v) {
       int y[8];
@@ -360,7 +357,12 @@ __global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 
         asm("prmt.b32 %0, %1, %2, %3;" : "=r"(a) : "r"(q < 4 ? xv[v].x : xv[v].y), "r"(nm),
             "r"((uint32_t)(q & 3) | (uint32_t)((q & 3) | 8) << 4 | 0x7600u));
         const int t = (q & 1) ? __dp2a_hi(a, (int)wp[4 * v + q / 2], 0) : __dp2a_lo(a, (int)wp[4 * v + q / 2], 0);
-        y[q] = (mad_wrap(t, rm, rnd) >> sh) + br[8 * v + q];
+        if (wide) {
+          const uint64_t addend = ((uint64_t)(uint32_t)br[8 * v + q] << 32) | 0x80000000ull;
+          y[q] = (int)(((long long)t * RM + (long long)addend) >> 32);
+        } else {
+          y[q] = (mad_wrap(t, rm, rnd) >> sh) + br[8 * v + q];
+        }
       }
       orow[32 * v] = make_uint2(pack4_sat_s8(y[0], y[1], y[2], y[3]), pack4_sat_s8(y[4], y[5], y[6], y[7]));
     }

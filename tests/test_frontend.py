@@ -1,10 +1,19 @@
 """torch -> anvil.graph for the nanoGPT family (CPU): capture patterns, quantization, and the float-path tolerance
 of the integer graph against the torch module (the model.measure method of the reference, anvil/model.py:302-342).
 
-Stated tolerances (max |dequantized int output - float output| in output LSBs, and RMS error / RMS output):
-    c1 block (n_embd 32, T 8):                 max <= 2 LSB,  rms <= 3 %
-    c2 2-layer model (vocab 64, n_embd 64):     max <= 8 LSB,  rms <= 8 %
-The float path runs on the dequantized integer input (input-quantisation free, as the reference measures).
+Stated tolerances (max |dequantized int output - float output| in output LSBs, RMS error / RMS output, and the
+gain sum(int * float) / sum(float^2)):
+    c1 block (n_embd 32, T 8):                  max <= 2 LSB,   rms <= 3 %
+    c2 2-layer model (vocab 64, n_embd 64):     max <= 8 LSB,   rms <= 8 %
+    c3 GPT-2-small block (T 1024), 2 seqs:      max <= 3.5 LSB, rms <= 5 %,  gain in [0.98, 1.02]
+                                                (measured 2.46 LSB, 3.7 %, 0.998)
+    c5 12-layer GPT-2-small (T 1024), 1 seq:    max <= 90 LSB,  rms <= 85 %, gain in [0.6, 1.1]
+                                                (measured 69 LSB, 77 %, 0.70; tests/test_gpu_configs.py, on the GPU)
+The float path runs on the dequantized integer input (input-quantisation free, as the reference measures). The c5
+figures are the reference recipe's own limit, not a kernel error (the integer outputs are bit-exact to the
+oracle): its int8 probabilities (one = 127) cannot hold the ~1/1024 attention weights that a randomly
+initialised model spreads over 1024 keys, and in c5 the residual stream starts from N(0, 0.02) embeddings, so the
+attention error is not diluted by a large input as it is in c3.
 """
 import numpy as np
 import pytest
@@ -14,7 +23,7 @@ from anvil import workloads as W
 from anvil.frontend import UnsupportedOpError, capture
 from oracle import interp
 
-TOL = {"c1": (2.0, 0.03), "c2": (8.0, 0.08)}
+TOL = {"c1": (2.0, 0.03), "c2": (8.0, 0.08), "c3": (3.5, 0.05)}
 
 
 def test_capture_matches_the_block_structure():
@@ -37,6 +46,30 @@ def test_model_capture_has_embedding_and_tied_head():
     head = fg.outputs[0]
     assert head.op == "linear" and head.attrs["bias"] is None
     assert np.array_equal(head.attrs["weight"], emb[0].attrs["wte"])     # tied
+
+
+def float_path_error(cm, x, ints_of=None):
+    """(max |error| in output LSBs, RMS error / RMS output, gain) of the first graph output on inputs x: the integer
+    graph (the oracle, or `ints_of(xq)` for another bit-exact path) against the float graph on the dequantized
+    input."""
+    if cm.meta[cm.inputs[0]][0] is not None:
+        xq = cm.quantize_input(x)
+        xin = xq * cm.scale(cm.inputs[0])
+    else:
+        xq = xin = x
+    o = cm.outputs[0]
+    ints = ints_of(xq) if ints_of else interp.run(cm.module, {cm.inputs[0]: xq}, cm.consts, batch=True).values[o]
+    r = cm.quantized.reference(xin)[o]
+    deq = np.asarray(ints) * cm.scale(o)
+    max_lsb = np.abs(deq - r).max() / cm.scale(o)
+    rms = np.sqrt(((deq - r) ** 2).mean() / (r ** 2).mean())
+    return float(max_lsb), float(rms), float((deq * r).sum() / (r * r).sum())
+
+
+def test_float_path_c3_block():
+    cm, gen = W.compile_config("c3")
+    max_lsb, rms, gain = float_path_error(cm, gen(2))
+    assert max_lsb <= TOL["c3"][0] and rms <= TOL["c3"][1] and 0.98 <= gain <= 1.02, (max_lsb, rms, gain)
 
 
 @pytest.mark.parametrize("name", ["c1", "c2"])

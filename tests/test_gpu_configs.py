@@ -41,6 +41,17 @@ def _oracle_by_sequence(module, inputs, consts):
     return {s: np.concatenate([r[s] for r in runs]) for s in runs[0] if s not in consts}
 
 
+_COMPILED = {}
+
+
+def _config(name):
+    """(CompiledModel, generator) of a BASELINE config, compiled once per test session (c5 takes a minute)."""
+    if name not in _COMPILED:
+        from anvil import workloads as W
+        _COMPILED[name] = W.compile_config(name)
+    return _COMPILED[name]
+
+
 def _launch_shapes(cm, batch):
     """(kind, describe tuple) of every launch of the program prepared on device 0 for `batch`."""
     prog = cm.program(batch)
@@ -172,13 +183,22 @@ def test_c3_block_64_sequences_sampled():
 def test_c5_model_one_sequence_every_logit():
     """Config c5 (12-layer GPT-2-small int8, vocab 50304, T 1024, seed 4): one sequence, all 1024 x 50304 logits
     vs the oracle."""
-    from anvil import workloads as W
-    cm, gen = W.compile_config("c5")
+    cm, gen = _config("c5")
     ids = np.asarray(gen(1))
     want = interp.run(cm.module, {cm.inputs[0]: ids}, cm.consts, batch=True)
     res = cm.run(ids, "cuda", quantized=True)
     for s in cm.outputs:
         _equal(res.ints[s], want.values[s], s)
+
+
+def test_c5_float_path_tolerance():
+    """Config c5's stated float-path tolerance (tests/test_frontend.py states and explains it): one sequence, the
+    integer logits from the GPU (bit-exact to the oracle, checked above) against the float model."""
+    from test_frontend import float_path_error
+    cm, gen = _config("c5")
+    max_lsb, rms, gain = float_path_error(cm, np.asarray(gen(1)),
+                                          lambda xq: cm.run(xq, "cuda", quantized=True).ints[cm.outputs[0]])
+    assert max_lsb <= 90 and rms <= 0.85 and 0.6 <= gain <= 1.1, (max_lsb, rms, gain)
 
 
 # --------------------------------------------------------------------------------------------- multi-GPU
