@@ -19,7 +19,8 @@ LIB_PATH = Path(__file__).resolve().parents[1] / "_lib" / "libanvil_cuda.so"
 
 OP_GEMM, OP_LUT, OP_LUT_MUL, OP_ADD_REQUANT, OP_NORM, OP_SOFTMAX, OP_TRANSPOSE, OP_EMBED, OP_ATTENTION, OP_COPY = \
     range(1, 11)
-F_CAUSAL, F_CHECKED, F_LUT, F_BIAS, F_CENTER, F_SIMT, F_BIAS_RND, F_RESIDUAL = 1, 2, 4, 8, 16, 32, 64, 128
+F_CAUSAL, F_CHECKED, F_LUT, F_BIAS, F_CENTER, F_SIMT, F_BIAS_RND, F_RESIDUAL, F_SPLIT = 1, 2, 4, 8, 16, 32, 64, 128, 256
+ABI_VERSION = 2
 LOC_CONST = 1 << 63
 LOC_NONE = (1 << 64) - 1
 
@@ -41,7 +42,7 @@ class AnvilOp(ctypes.Structure):
                 ("dims", ctypes.c_int64 * 8), ("strides", ctypes.c_int64 * 8), ("off", ctypes.c_uint64 * 8),
                 ("mult", ctypes.c_int64), ("shift", ctypes.c_int64), ("ma", ctypes.c_int64), ("mb", ctypes.c_int64),
                 ("one", ctypes.c_int64), ("ss_shift", ctypes.c_int64), ("ss_init", ctypes.c_int64),
-                ("mult2", ctypes.c_int64), ("shift2", ctypes.c_int64)]
+                ("mult2", ctypes.c_int64), ("shift2", ctypes.c_int64), ("aux", ctypes.c_int64 * 8)]
 
 
 class AnvilIO(ctypes.Structure):
@@ -89,8 +90,8 @@ def load_library(path: str | os.PathLike | None = None):
             f = getattr(lib, name)
             f.argtypes = args
             f.restype = res
-        if lib.anvil_abi_version() != 1:
-            raise ImportError(f"{p}: ABI version {lib.anvil_abi_version()} != 1")
+        if lib.anvil_abi_version() != ABI_VERSION:
+            raise ImportError(f"{p}: ABI version {lib.anvil_abi_version()} != {ABI_VERSION}")
         if path is None:
             _lib = lib
         return lib

@@ -115,7 +115,7 @@ struct Launch {
   bool tc = false;
   bool pair = false;
   int bn = 0;
-  CUtensorMap mapA, mapB, mapC;
+  CUtensorMap mapA, mapB, mapC, mapC2;   // mapC2: the transposed part of a split output
   GemmParams gp;
   AttnParams ap;
   int hd = 0;
@@ -349,14 +349,16 @@ struct TileChoice {
   bool pair;
 };
 
-static TileChoice choose_tiles(int64_t batch, int64_t M, int64_t N, int64_t K, int sms, int pair_cap, bool res) {
+static TileChoice choose_tiles(int64_t batch, int64_t M, int64_t N, int64_t K, int sms, int pair_cap, bool res,
+                               bool bn256_only = false) {
   struct Cand { int bn; bool pair; double weight; };
   const Cand cands[4] = {{256, true, 1.0}, {256, false, 1.1}, {128, false, 1.2}, {64, false, 1.45}};
   TileChoice best = {256, false};
   double best_cost = -1;
   for (const Cand &c : cands) {
     if (c.pair && (pair_cap <= 0 || M < 4 * TC_BM || (res && K < 2048) || N <= 128)) continue;
-    if (!c.pair && c.bn > 64 && N <= c.bn / 2) continue;            // a narrower tile holds every column
+    if (!c.pair && c.bn > 64 && N <= c.bn / 2 && !bn256_only) continue;   // a narrower tile holds every column
+    if (bn256_only && c.bn != 256) continue;
     const int64_t rows = c.pair ? 2 * TC_BM : TC_BM;
     const int64_t tiles = batch * ((M + rows - 1) / rows) * ((N + c.bn - 1) / c.bn);
     const int64_t cap = c.pair ? pair_cap : sms;
@@ -376,7 +378,28 @@ static TileChoice choose_tiles(int64_t batch, int64_t M, int64_t N, int64_t K, i
 static int gemm_out_map(Launch &L) {
   GemmParams &p = L.gp;
   memset(&L.mapC, 0, sizeof L.mapC);
+  memset(&L.mapC2, 0, sizeof L.mapC2);
   p.tma_store = 0;
+  if (p.split_c) {
+    // split output: columns [0, split_r) row-major in OUT (row stride o_rstride), the rest head-major transposed
+    // in OUT2 (group o_group2); the caller checked the shapes and alignments
+    if (!L.tc || L.bn != 256) return fail(ANVIL_E_BAD_ARG, "op %d: a split gemm needs 256-column tcgen05 tiles",
+                                          p.op_index);
+    const uint64_t cdims[2] = {(uint64_t)p.split_r, (uint64_t)p.M};
+    const uint64_t cstr[1] = {(uint64_t)p.o_rstride};
+    const uint32_t cbox[2] = {64, 32};
+    int rc;
+    if (p.split_r > 0 && (rc = make_map(&L.mapC, p.out, 2, cdims, cstr, cbox, CU_TENSOR_MAP_SWIZZLE_64B))) return rc;
+    const int64_t T = p.o_group2, N2 = p.N - p.split_r;
+    if (N2 > 0) {
+      const uint64_t tdims[3] = {(uint64_t)T, (uint64_t)N2, (uint64_t)(p.M / T)};
+      const uint64_t tstr[2] = {(uint64_t)T, (uint64_t)(N2 * T)};
+      const uint32_t tbox[3] = {32, 64, 1};
+      if ((rc = make_map(&L.mapC2, p.out2, 3, tdims, tstr, tbox, CU_TENSOR_MAP_SWIZZLE_NONE))) return rc;
+    }
+    p.tma_store = 1;
+    return ANVIL_OK;
+  }
   if (!L.tc || L.bn != 256 || p.out_bytes != 1 || !aligned16(p.out) || p.M > (1ll << 31) - 1 ||
       p.N > (1ll << 31) - 1)
     return ANVIL_OK;
@@ -429,7 +452,8 @@ static int tile_magics(GemmParams &p, int op_index) {
 // Tile shape, tile count, tile-decode magics and tensor maps of a tcgen05 GEMM whose GemmParams are filled in.
 static int tc_tiles(anvil_model *m, Launch &L) {
   GemmParams &p = L.gp;
-  const TileChoice tc = choose_tiles(p.batch, p.M, p.N, p.K, m->sms, pair_clusters(m), p.res != nullptr);
+  const TileChoice tc = choose_tiles(p.batch, p.M, p.N, p.K, m->sms, pair_clusters(m), p.res != nullptr,
+                                     p.split_c != 0);
   L.bn = tc.bn;
   L.pair = tc.pair;
   const int64_t tile_rows = L.pair ? 2 * TC_BM : TC_BM;
@@ -505,11 +529,39 @@ static int prepare_gemm(anvil_model *m, Launch &L) {
   p.check = (op.flags & ANVIL_F_CHECKED) ? 1 : 0;
   p.flags = m->flags;
   p.op_index = op.op_index;
+  if (op.flags & ANVIL_F_SPLIT) {
+    // several linears of one input as one GEMM: dims[4] = chunk columns C, dims[5] = row-major columns R,
+    // dims[6] = the transposed part's row group T; aux[c] = (M_c << 8) | s_c; off[6] = the transposed part
+    const int64_t C = op.dims[4], Rr = op.dims[5], T = op.dims[6];
+    const int64_t nch = C > 0 ? N / C : 0;
+    if ((op.flags & (ANVIL_F_CHECKED | ANVIL_F_LUT | ANVIL_F_RESIDUAL | ANVIL_F_SIMT)) || batch != 1 ||
+        op.out_bytes != 1 || C <= 0 || C % 256 || N % C || nch > 8 || Rr < 0 || Rr > N || Rr % C ||
+        o_rs < Rr || o_rs % 16 || o_cs != 1 || op.strides[4] != 0 ||
+        (Rr < N && (T <= 0 || T % 32 || M % T || T > (1ll << 31) - 1)))
+      return fail(ANVIL_E_BAD_ARG, "op %d: bad split gemm", op.op_index);
+    for (int64_t c = 0; c < nch; ++c) {
+      const int64_t mc = op.aux[c] >> 8, sc = op.aux[c] & 255;
+      if (mc < 0 || mc > 0x7fffffffll || sc > 31) return fail(ANVIL_E_BAD_ARG, "op %d: bad split chunk %lld",
+                                                              op.op_index, (long long)c);
+      p.smult[c] = (int)mc;
+      p.sshift[c] = (int)sc;
+    }
+    if (Rr < N && (rc = resolve(m, op, 6, (uint64_t)M * (N - Rr), &L.ptr[6]))) return rc;
+    p.split_c = (int)C;
+    p.split_r = (int)Rr;
+    p.o_group2 = T;
+    p.out2 = L.ptr[6];
+    if (!aligned16(p.out) || (p.out2 && !aligned16(p.out2)))
+      return fail(ANVIL_E_BAD_ARG, "op %d: split gemm outputs must be 16-byte aligned", op.op_index);
+  }
   const bool tc_ok = !(op.flags & ANVIL_F_SIMT) && K % 16 == 0 && a_bs % 16 == 0 && bt_bs % 16 == 0 &&
                      aligned16(p.A) && aligned16(p.BT) && M <= (1ll << 31) - 256 && N <= (1ll << 31) - 256 &&
                      batch <= (1ll << 31) - 1;
   L.tc = tc_ok;
-  if (!tc_ok) return ANVIL_OK;
+  if (!tc_ok) {
+    if (p.split_c) return fail(ANVIL_E_BAD_ARG, "op %d: a split gemm needs the tcgen05 path", op.op_index);
+    return ANVIL_OK;
+  }
   return tc_tiles(m, L);
 }
 
@@ -687,19 +739,19 @@ static int launch_op(anvil_model *m, Launch &L) {
         cudaError_t e;
         if (op.out_bytes == 1)
           e = cudaLaunchKernelEx(&cfg, p.res ? qgemm_tc_kernel<256, 1, true, true> : qgemm_tc_kernel<256, 1, false, true>,
-                                 L.mapA, L.mapB, L.mapC, p);
+                                 L.mapA, L.mapB, L.mapC, L.mapC2, p);
         else
           e = cudaLaunchKernelEx(&cfg, p.res ? qgemm_tc_kernel<256, 2, true, true> : qgemm_tc_kernel<256, 2, false, true>,
-                                 L.mapA, L.mapB, L.mapC, p);
+                                 L.mapA, L.mapB, L.mapC, L.mapC2, p);
         if (e != cudaSuccess) return fail(ANVIL_E_CUDA, "op %d: pair gemm launch failed: %s", oi, cudaGetErrorString(e));
       } else if (L.tc) {
         const int grid = (int)std::min<int64_t>(p.tiles, m->sms);
 #define TC_LAUNCH(BN, OB)                                                                                       \
   do {                                                                                                          \
     if (p.res)                                                                                                  \
-      qgemm_tc_kernel<BN, OB, true><<<grid, TC_THREADS, TcCfg<BN>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, p); \
+      qgemm_tc_kernel<BN, OB, true><<<grid, TC_THREADS, TcCfg<BN>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, L.mapC2, p); \
     else                                                                                                        \
-      qgemm_tc_kernel<BN, OB, false><<<grid, TC_THREADS, TcCfg<BN>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, p);\
+      qgemm_tc_kernel<BN, OB, false><<<grid, TC_THREADS, TcCfg<BN>::SMEM_BYTES, st>>>(L.mapA, L.mapB, L.mapC, L.mapC2, p);\
   } while (0)
         if (L.bn == 64) { if (op.out_bytes == 1) TC_LAUNCH(64, 1); else TC_LAUNCH(64, 2); }
         else if (L.bn == 128) { if (op.out_bytes == 1) TC_LAUNCH(128, 1); else TC_LAUNCH(128, 2); }

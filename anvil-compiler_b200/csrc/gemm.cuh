@@ -44,6 +44,13 @@ struct GemmParams {
   // tc path, BN = 256, i8 output through shared-memory staging and TMA tile stores: 1 = row-major; 2 = the
   // head-major transposed layout (element (r, c) at (r / o_group) * o_gstride + c * o_group + r % o_group)
   int tma_store;
+  // split output (several linears of one input as one GEMM, tc path, BN = 256): the N columns are chunks of split_c
+  // columns, chunk c requantised with (smult[c], sshift[c]); columns below split_r leave row-major through the
+  // output map, the rest head-major transposed (group o_group2) through the second output map, column - split_r
+  int split_c, split_r;
+  int64_t o_group2;
+  void *out2;
+  int smult[8], sshift[8];
 };
 
 // y -> the fused residual add's result (32-bit exact under the static int32 proof)
@@ -178,7 +185,7 @@ struct TcCfg {
   static constexpr int BAR_OFF = STG_OFF + STG_BYTES;
   static constexpr int MISC_OFF = BAR_OFF + (2 * STAGES + 4) * 8;
   static constexpr int BST_OFF = MISC_OFF + 16;
-  static constexpr int SMEM_BYTES = BST_OFF + TC_EPI_WARPS * 128 + 1024;  // + 1 KB slack to align the ring
+  static constexpr int SMEM_BYTES = BST_OFF + TC_EPI_WARPS * 64 + 1024;   // + 1 KB slack to align the ring
 };
 
 // Load 32 consecutive int8 / int16 values of a row (vector loads when the chunk is whole and aligned).
@@ -299,7 +306,8 @@ __device__ __forceinline__ void store_row32(typename IntOf<OB>::T *dst, const in
 template <int BN, int OB, bool RES, bool PAIR = false>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2,
+                    const GemmParams p) {
   using Cfg = TcCfg<BN, PAIR>;
   constexpr int TMR = PAIR ? 2 * TC_BM : TC_BM;       // rows of one tile
   extern __shared__ uint8_t smem_raw[];
@@ -335,6 +343,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     if (p.tma_store) prefetch_tmap(&tmC);
+    if (p.split_c) prefetch_tmap(&tmC2);
   }
   if (p.lut)
     for (int i = threadIdx.x; i < 32 * 256; i += TC_THREADS) lut_r[i] = p.lut[i >> 5];
@@ -443,17 +452,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr int NSC = Cfg::NSC;
     const int lane_base = 32 * (warp & 3);
     const int cq = (warp - 2) >> 2;
-    int32_t *bslot = bst + (warp - 2) * 32;                   // 16 columns x (int32 or 64-bit) staged bias
+    int32_t *bslot = bst + (warp - 2) * 16;
     int acc = 0;
     uint32_t aphase = 0;
     constexpr int lo = OB == 1 ? -128 : -32768, hi = OB == 1 ? 127 : 32767;
     const int32_t *lt = p.lut ? lut_r + lane : nullptr;       // this lane's copy: lt[32 e] = lut[e]
-    const int m32 = (int)p.mult, sh = p.shift, rnd = sh ? 1 << (sh - 1) : 0;
-    // With s >= 1 and M < 2^(s-1), Mw = M * 2^(32-s) fits int32 and the high word of the 64-bit
-    // acc * Mw + (bias*M + 2^(s-1)) * 2^(32-s) is (acc * M + bias*M + 2^(s-1)) >> s exactly: one wide multiply-add
-    // per output instead of a multiply-add and a shift (the shift being on the busier ALU pipe)
-    const bool wide = !p.check && sh >= 1 && p.mult >= 0 && p.mult < (1ll << (sh - 1));
-    const int mw = wide ? (int)((uint32_t)p.mult << (32 - sh)) : 0;
+    // the requant constants (per tile for a split output, whose chunks have their own)
+    int m32 = 0, sh = 0, rnd = 0, mw = 0;
+    bool wide = false;
+    // Without a bias, with s >= 1 and M < 2^(s-1), Mw = M * 2^(32-s) fits int32 and the high word of the 64-bit
+    // acc * Mw + 2^31 is (acc * M + 2^(s-1)) >> s exactly: one wide multiply-add per output instead of a
+    // multiply-add and a shift (the shift being on the busier ALU pipe)
+    auto set_requant = [&](long long mult, int shift) {
+      m32 = (int)mult;
+      sh = shift;
+      rnd = sh ? 1 << (sh - 1) : 0;
+      wide = !p.check && !p.bias && sh >= 1 && mult >= 0 && mult < (1ll << (sh - 1));
+      mw = wide ? (int)((uint32_t)mult << (32 - sh)) : 0;
+    };
+    set_requant(p.mult, p.shift);
     // fused residual with i8 y and i8 residual: both enter biased by 128 (u = x + 128, one byte extract each),
     // and -128 (Ma + Mb) folds into the rounding constant; the sum is formed mod 2^32 and is exact because the
     // static int32 proof bounds the true value
@@ -464,7 +481,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // leave as one tile store, edges clipped by the tensor map. Row-major mode: row r at r*64 bytes, 16-byte chunk
     // c at position c ^ ((r >> 1) & 3) (the 64-byte swizzle of the output map). Transposed mode: 64 column-rows of
     // 32 bytes, lane = byte.
-    const int tmode = p.tma_store;
+    int tmode = p.tma_store;
     const bool tma_st = tmode != 0;
     uint8_t *stg_w = smem + Cfg::STG_OFF + (warp - 2) * Cfg::STG_WARP;
     uint8_t *stg = stg_w + lane * Cfg::COLS;
@@ -479,6 +496,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int64_t row = row0 + lane_base + lane;
       const bool row_ok = row < p.M;
       const int64_t cbase = nb * BN + cq * Cfg::COLS;
+      const CUtensorMap *omap = &tmC;                 // this tile's output map, column offset and row group
+      int64_t ocol = cbase, ogrp = p.o_group;
+      if (p.split_c) {
+        const int64_t c0t = (int64_t)nb * BN;
+        const int ch = (int)(c0t / p.split_c);
+        set_requant(p.smult[ch], p.sshift[ch]);
+        if (c0t >= p.split_r) {
+          tmode = 2;
+          omap = &tmC2;
+          ocol = cbase - p.split_r;
+          ogrp = p.o_group2;
+        } else {
+          tmode = 1;
+        }
+      }
       uint4 rcur = make_uint4(0, 0, 0, 0), rnxt = make_uint4(0, 0, 0, 0);
       bool rcur_ok = false, rnxt_ok = false;
       auto prefetch = [&](int sc, uint4 &dst, bool &ok) {
@@ -525,23 +557,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           // exact; a bias arrives pre-folded as bias*M + 2^(s-1) (ANVIL_F_BIAS_RND)
           int y[16];
           if (wide) {
-            long long ad[16];                           // (bias*M + 2^(s-1)) * 2^(32-s), or 2^31 without a bias
-            if (p.bias) {
-              __syncwarp();
-              if (lane < 16) reinterpret_cast<long long *>(bslot)[lane] = (long long)bcur << (32 - sh);
-              __syncwarp();
 #pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                const longlong2 b2 = reinterpret_cast<const longlong2 *>(bslot)[q];
-                ad[2 * q] = b2.x;
-                ad[2 * q + 1] = b2.y;
-              }
-            } else {
-#pragma unroll
-              for (int q = 0; q < 16; ++q) ad[q] = 0x80000000ll;
-            }
-#pragma unroll
-            for (int q = 0; q < 16; ++q) y[q] = (int)(((long long)r[q] * mw + ad[q]) >> 32);
+            for (int q = 0; q < 16; ++q) y[q] = (int)(((long long)r[q] * mw + 0x80000000ll) >> 32);
           } else {
             int br[16];
             if (p.bias) {
@@ -641,13 +658,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         __syncwarp();
         if (lane == 0 && row0 + lane_base < p.M) {    // a pair's odd CTA may have no rows left in the last tile
           const int64_t r0 = row0 + lane_base;
-          const int c0 = (int)cbase;
+          const int c0 = (int)ocol;
           if (tmode == 2) {                            // r0 and the group (T) are below 2^31
-            const uint32_t grp = (uint32_t)p.o_group, gq = (uint32_t)r0 / grp;
-            tma_store_3d(&tmC, stg_w, (int)((uint32_t)r0 - gq * grp), c0, (int)gq);
+            const uint32_t grp = (uint32_t)ogrp, gq = (uint32_t)r0 / grp;
+            tma_store_3d(omap, stg_w, (int)((uint32_t)r0 - gq * grp), c0, (int)gq);
           }
-          else if (p.batch > 1) tma_store_3d(&tmC, stg_w, c0, (int)r0, (int)bb);
-          else tma_store_2d(&tmC, stg_w, c0, (int)r0);
+          else if (p.batch > 1) tma_store_3d(omap, stg_w, c0, (int)r0, (int)bb);
+          else tma_store_2d(omap, stg_w, c0, (int)r0);
           bulk_commit();
         }
       }

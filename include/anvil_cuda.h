@@ -26,7 +26,7 @@ extern "C" {
 #define ANVIL_API
 #endif
 
-#define ANVIL_ABI_VERSION 1
+#define ANVIL_ABI_VERSION 2
 
 /* status codes (mapped to the reference's exception types by anvil/runtime/cuda.py) */
 #define ANVIL_OK 0
@@ -70,6 +70,11 @@ enum anvil_op_kind {
 #define ANVIL_F_RESIDUAL 128u /* gemm: fused add_requant with off[5] = RES ((M, N) row-major, in2_bytes):
                                  out = clamp((res*ma + y*mb + 2^(shift2-1)) >> shift2), y the requant result
                                  clamped to in_bytes' range; unchecked, unbatched, row-major output only     */
+#define ANVIL_F_SPLIT 256u    /* gemm: several linears of one input as one GEMM (the q, k, v projections):
+                                 dims[4] = C columns per chunk (a multiple of 256), chunk c requantised with
+                                 aux[c] = (M_c << 8) | s_c; columns below dims[5] = R go row-major to OUT (row
+                                 stride strides[3]), the rest head-major transposed (the ATTENTION VT layout,
+                                 row group dims[6] = T) to off[6]; unchecked, unbatched, i8, no LUT / residual  */
 
 /* One lowered kernel launch. Field meaning per kind (all sizes in elements, offsets in bytes):
  *   GEMM        dims  = {batch, M, N, K}; strides = {a_batch, bt_batch (0: shared weight), out_batch,
@@ -105,6 +110,7 @@ typedef struct anvil_op {
   int64_t strides[8];
   uint64_t off[8];
   int64_t mult, shift, ma, mb, one, ss_shift, ss_init, mult2, shift2;
+  int64_t aux[8];          /* GEMM with ANVIL_F_SPLIT: (M_c << 8) | s_c of output chunk c */
 } anvil_op;
 
 /* A host buffer bound to an arena range for one run (graph inputs and outputs). */

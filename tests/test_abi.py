@@ -48,7 +48,7 @@ def test_struct_layout_matches_header(tmp_path):
 
 def test_calls_fail_cleanly_without_a_device():
     lib = C.load_library()
-    assert lib.anvil_abi_version() == 1
+    assert lib.anvil_abi_version() == C.ABI_VERSION
     if C.device_count() > 0:
         pytest.skip("a GPU is visible")
     h = ctypes.c_void_p()

@@ -11,7 +11,7 @@ against the plain definitions (CPU). Each test names the kernel code that uses t
   64-bit checks; and the pass-B division floor(n / S) = umulhi(n, m) >> (lg - 1) it feeds.
 - the wide requant (rowops.cuh norm_row_kernel, attention.cuh scores, gemm.cuh epilogue): with 1 <= s <= 32 and
   0 <= M < 2^(s-1) (any M when s = 32), the high word of the 64-bit a * (M 2^(32-s)) + c 2^(32-s) + b 2^32 is
-  ((a M + c) >> s) + b for every int32 a and c = 2^(s-1) (or c = bias M + 2^(s-1) in the GEMM).
+  ((a M + c) >> s) + b for every int32 a and c = 2^(s-1) (b = 0 in the GEMM and the scores).
 """
 import random
 
