@@ -322,6 +322,10 @@ class Lowering:
             return
         if id(op) in self.attn_o:
             return self._attention(*self.attn_o[id(op)])
+        if id(op) in self.qkv:             # one launch for the three projections, at the first of them
+            if id(op.result) not in self.views:
+                self._qkv_gemm(self.qkv[id(op)])
+            return
         a = self.views[id(op.a)]
         b = self.views[id(op.b)]
         t = g.qt(op.result)
@@ -434,6 +438,45 @@ class Lowering:
     _QMatmulOp = _gemm
     _QLinearOp = _gemm
 
+    def _qkv_gemm(self, group):
+        """q, k, v = x @ Wq, x @ Wk, x @ Wv (each with its own requant and bias) as one GEMM over the concatenated
+        weights, reading x once: q and k land side by side in one row-major buffer (row stride 2C, read in place by
+        the fused attention), v head-major transposed (the attention's V^T operand)."""
+        q, k, v = group
+        a = self.contig(self.views[id(q.a)], f"{q.sym_str}.a")
+        K, Cw = g.qt(q.b).dims
+        Mt = math.prod(a.shape[:-1])
+        T = self.vt_gemm[id(v)]
+        ws = [self.const_array(self.views[id(o.b)]) for o in group]
+        bt = np.ascontiguousarray(np.concatenate([w.T for w in ws]), dtype=np.int8)
+        bt_slot = ("const", self.pool.add(("qkv_w",) + tuple(self.views[id(o.b)].root for o in group), bt))
+        flags = C.F_SPLIT
+        bias_slot = None
+        if any(o.bias is not None for o in group):
+            parts = []
+            for o in group:
+                bq = self.const_array(self.views[id(o.bias)]) if o.bias is not None else np.zeros(Cw, np.int64)
+                parts.append(bq * int(o.M) + ((1 << (o.s - 1)) if o.s else 0))
+            bias_slot = ("const", self.pool.add(("qkv_b",) + tuple(
+                (self.views[id(o.bias)].root if o.bias is not None else None, int(o.M), int(o.s)) for o in group),
+                np.ascontiguousarray(np.concatenate(parts), dtype=np.int32)))
+            flags |= C.F_BIAS | C.F_BIAS_RND
+        lead = a.shape[:-1]
+        label = "+".join(o.sym_str or "qlinear" for o in group)
+        qk = self.new_view(f"{q.sym_str}+{k.sym_str}", lead + (2 * Cw,), "i8")
+        vb = self.new_view(v.sym_str or "v", lead + (Cw,), "i8")
+        self.emit(C.OP_GEMM, [self.act_slot(a), bt_slot, self.act_slot(qk), None, bias_slot, None,
+                              self.act_slot(vb)],
+                  {"dims": [1, Mt, 3 * Cw, K, Cw, 2 * Cw, T], "strides": [0, 0, Mt * 2 * Cw, 2 * Cw, 0, 0, 1],
+                   "mult": q.M, "shift": q.s, "out_bytes": 1, "flags": flags,
+                   "aux": [(int(o.M) << 8) | int(o.s) for o in group]}, label, [a.root], [qk.root, vb.root],
+                  {"ops": 2 * Mt * 3 * Cw * K, "bytes": Mt * K + 3 * Cw * K + Mt * 3 * Cw})
+        qs = qk.strides[:-1] + (1,)
+        self.views[id(q.result)] = View(qk.root, False, lead + (Cw,), qs, 0, "i8")
+        self.views[id(k.result)] = View(qk.root, False, lead + (Cw,), qs, Cw, "i8")
+        self.views[id(v.result)] = View(vb.root, False, vb.shape, (Cw * T, 1, T), 0, "i8")
+        self.fused.append(f"{label}:qkv_split")
+
     # ---- fused attention
     def _attention(self, sop, pop, oop):
         label = oop.sym_str or "attention"
@@ -471,7 +514,7 @@ class Lowering:
     def detect_fusions(self):
         """Find head-batched qk^T -> softmax_lut -> p@v chains the fused attention kernel can run, and the V
         projections that can write V^T for them."""
-        self.attn, self.attn_o, self.vt_gemm = {}, {}, {}
+        self.attn, self.attn_o, self.vt_gemm, self.qkv = {}, {}, {}, {}
         if not self.fuse or self.checked:
             return
         uses = self.uses
@@ -511,6 +554,37 @@ class Lowering:
                             and len(g.qt(vop.b).dims) == 2 and g.qt(vop.result).dims == (T2, H * hd) \
                             and g.qt(vop.result).dtype == "i8":
                         self.vt_gemm[id(vop)] = T2
+        # the q, k and v projections of one attention, linears of one input, as one split-output GEMM
+        for sop, pop, oop in list(self.attn_o.values()):
+            group = (self._layout_source(sop.a), self._layout_source(sop.b), self._layout_source(oop.b))
+            if self._splittable(group):
+                for op in group:
+                    self.qkv[id(op)] = group
+
+    @staticmethod
+    def _layout_source(v):
+        """The op producing value v, looking through reshapes and transposes."""
+        op = v.owner
+        while isinstance(op, (g.ReshapeOp, g.TransposeOp)):
+            op = op.x.owner
+        return op
+
+    def _splittable(self, group) -> bool:
+        """q, k, v: linears of one input with constant 2-D weights, equal widths that are whole 256-column tiles,
+        i8 results that are no graph outputs, v feeding the attention transposed (its V^T epilogue), on the
+        tcgen05 path."""
+        q, k, v = group
+        if len({id(o) for o in group}) != 3 or id(v) not in self.vt_gemm or id(q) in self.vt_gemm or \
+                id(k) in self.vt_gemm or self.gemm_mode == "simt":
+            return False
+        for o in group:
+            if not isinstance(o, (g.QLinearOp, g.QMatmulOp)) or o.lut is not None or o.a is not q.a or \
+                    not isinstance(o.b.owner, g.ConstOp) or len(g.qt(o.b).dims) != 2 or \
+                    g.qt(o.result).dtype != "i8" or id(o.result) in self.out_ids:
+                return False
+        dims = [g.qt(o.b).dims for o in group]
+        K, C = dims[0]
+        return all(d == (K, C) for d in dims) and C % 256 == 0 and K % 16 == 0
 
     # ---- memory-bound ops
     def _act(self, value, label):
@@ -661,6 +735,8 @@ def lower_program(module, consts: dict, pool: ConstPool, batch: int, keep="outpu
                 o.off[j] = plan.addresses[s[1]] + int(s[2])
         for k in ("mult", "shift", "ma", "mb", "one", "ss_shift", "ss_init", "mult2", "shift2"):
             setattr(o, k, int(f.get(k, 0)))
+        for j, v in enumerate(f.get("aux", [])):
+            o.aux[j] = int(v)
         ops.append(o)
     inputs = {}
     for op in func.ops:

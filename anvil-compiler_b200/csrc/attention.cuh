@@ -309,11 +309,6 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     const int r = lane_base + lane;
     const int m1 = (int)p.m1;
     const int rnd1 = (int)round_term(p.s1);
-    // With s1 >= 1 and m1 < 2^(s1-1), M1w = m1 * 2^(32-s1) fits int32 and the high word of the 64-bit
-    // acc * M1w + 2^31 is (acc * m1 + 2^(s1-1)) >> s1 exactly: one wide multiply-add instead of a multiply-add and
-    // a shift (and off the ALU pipe)
-    const bool wide1 = p.s1 >= 1 && p.m1 >= 0 && p.m1 < (1ll << (p.s1 - 1));
-    const int m1w = wide1 ? (int)((uint32_t)p.m1 << (32 - p.s1)) : 0;
     int32_t *red_max = reinterpret_cast<int32_t *>(smem + Cfg::OFF_RED);   // [4][128] partial row max
     int32_t *red_sum = red_max + 512;                                          // [4][128] partial row sum
     const int lcopy = lane % Cfg::LUT_COPIES;
@@ -379,8 +374,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         // saturating pack.
         int v[32];
 #pragma unroll
-        for (int q = 0; q < 32; ++q)
-          v[q] = wide1 ? (int)(((long long)acc[q] * m1w + 0x80000000ll) >> 32) : mad_wrap(acc[q], m1, rnd1) >> p.s1;
+        for (int q = 0; q < 32; ++q) v[q] = mad_wrap(acc[q], m1, rnd1) >> p.s1;
         if (__all_sync(0xffffffffu, cb + 32 <= kept)) {
 #pragma unroll
           for (int q = 0; q < 32; ++q) mx = max(mx, v[q]);

@@ -458,17 +458,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr int lo = OB == 1 ? -128 : -32768, hi = OB == 1 ? 127 : 32767;
     const int32_t *lt = p.lut ? lut_r + lane : nullptr;       // this lane's copy: lt[32 e] = lut[e]
     // the requant constants (per tile for a split output, whose chunks have their own)
-    int m32 = 0, sh = 0, rnd = 0, mw = 0;
-    bool wide = false;
-    // Without a bias, with s >= 1 and M < 2^(s-1), Mw = M * 2^(32-s) fits int32 and the high word of the 64-bit
-    // acc * Mw + 2^31 is (acc * M + 2^(s-1)) >> s exactly: one wide multiply-add per output instead of a
-    // multiply-add and a shift (the shift being on the busier ALU pipe)
+    int m32 = 0, sh = 0, rnd = 0;
     auto set_requant = [&](long long mult, int shift) {
       m32 = (int)mult;
       sh = shift;
       rnd = sh ? 1 << (sh - 1) : 0;
-      wide = !p.check && !p.bias && sh >= 1 && mult >= 0 && mult < (1ll << (sh - 1));
-      mw = wide ? (int)((uint32_t)mult << (32 - sh)) : 0;
     };
     set_requant(p.mult, p.shift);
     // fused residual with i8 y and i8 residual: both enter biased by 128 (u = x + 128, one byte extract each),
@@ -555,28 +549,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         } else {
           // the static int32 proof holds: (acc [+ bias]) * M + 2^(s-1) fits int32, so 32-bit wrap-free math is
           // exact; a bias arrives pre-folded as bias*M + 2^(s-1) (ANVIL_F_BIAS_RND)
-          int y[16];
-          if (wide) {
+          int br[16];
+          if (p.bias) {
+            __syncwarp();
+            if (lane < 16) bslot[lane] = bcur;
+            __syncwarp();
 #pragma unroll
-            for (int q = 0; q < 16; ++q) y[q] = (int)(((long long)r[q] * mw + 0x80000000ll) >> 32);
-          } else {
-            int br[16];
-            if (p.bias) {
-              __syncwarp();
-              if (lane < 16) bslot[lane] = bcur;
-              __syncwarp();
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int4 b4 = reinterpret_cast<const int4 *>(bslot)[q];
-                br[4 * q] = b4.x; br[4 * q + 1] = b4.y; br[4 * q + 2] = b4.z; br[4 * q + 3] = b4.w;
-              }
-            } else {
-#pragma unroll
-              for (int q = 0; q < 16; ++q) br[q] = rnd;
+            for (int q = 0; q < 4; ++q) {
+              const int4 b4 = reinterpret_cast<const int4 *>(bslot)[q];
+              br[4 * q] = b4.x; br[4 * q + 1] = b4.y; br[4 * q + 2] = b4.z; br[4 * q + 3] = b4.w;
             }
+          } else {
 #pragma unroll
-            for (int q = 0; q < 16; ++q) y[q] = mad_wrap(r[q], m32, br[q]) >> sh;
+            for (int q = 0; q < 16; ++q) br[q] = rnd;
           }
+          int y[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) y[q] = mad_wrap(r[q], m32, br[q]) >> sh;
           if (!RES) {
             if (OB == 1 && lt) {
               // saturate four at a time, bias the bytes by 128 and look each up in this lane's LUT copy

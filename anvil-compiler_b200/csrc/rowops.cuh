@@ -342,11 +342,6 @@ __global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 
     const int sh = s + k;
     const int rnd = sh ? 1 << (sh - 1) : 0;
     const uint32_t nm = (uint32_t)(-mean) << 16;
-    // With 1 <= sh <= 32 and 0 <= rm < 2^(sh-1), RM = rm * 2^(32-sh) fits int32 and the high word of the 64-bit
-    // t * RM + bias * 2^32 + 2^31 is ((t * rm + 2^(sh-1)) >> sh) + bias exactly: one wide multiply-add does the
-    // rescale, the rounding shift and the bias. Other rows take the 32-bit multiply-add, shift and add.
-    const bool wide = sh >= 1 && sh <= 32 && rm >= 0 && (sh == 32 || rm < (1 << (sh - 1)));
-    const int RM = wide ? (int)((uint32_t)rm << (32 - sh)) : 0;
 #pragma unroll
     for (int v = 0; v < NV8; ++v) {
       int y[8];
@@ -357,12 +352,7 @@ __global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 
         asm("prmt.b32 %0, %1, %2, %3;" : "=r"(a) : "r"(q < 4 ? xv[v].x : xv[v].y), "r"(nm),
             "r"((uint32_t)(q & 3) | (uint32_t)((q & 3) | 8) << 4 | 0x7600u));
         const int t = (q & 1) ? __dp2a_hi(a, (int)wp[4 * v + q / 2], 0) : __dp2a_lo(a, (int)wp[4 * v + q / 2], 0);
-        if (wide) {
-          const uint64_t addend = ((uint64_t)(uint32_t)br[8 * v + q] << 32) | 0x80000000ull;
-          y[q] = (int)(((long long)t * RM + (long long)addend) >> 32);
-        } else {
-          y[q] = (mad_wrap(t, rm, rnd) >> sh) + br[8 * v + q];
-        }
+        y[q] = (mad_wrap(t, rm, rnd) >> sh) + br[8 * v + q];
       }
       orow[32 * v] = make_uint2(pack4_sat_s8(y[0], y[1], y[2], y[3]), pack4_sat_s8(y[4], y[5], y[6], y[7]));
     }

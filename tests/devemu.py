@@ -47,6 +47,8 @@ class Emu:
             getattr(self, "k%d" % o.kind)(o)
 
     def k1(self, o):                                    # GEMM
+        if o.flags & C.F_SPLIT:
+            return self._split_gemm(o)
         batch, M, N, K = (int(o.dims[i]) for i in range(4))
         abs_, bbs, obs, ors = (int(o.strides[i]) for i in range(4))
         grp, gst, cst = int(o.strides[4]) or M, int(o.strides[5]), int(o.strides[6]) or 1
@@ -78,6 +80,33 @@ class Emu:
             flat = mem[base:].view(DT[o.out_bytes])
             assert idx.max() < flat.size, "write outside region"
             flat[idx] = v.astype(DT[o.out_bytes])
+
+    def _split_gemm(self, o):
+        """Several linears as one GEMM: chunk c of dims[4] columns requantised with aux[c]; columns below dims[5]
+        row-major to off[2] (row stride strides[3]), the rest head-major transposed (group dims[6]) to off[6]."""
+        M, N, K, Cw, R, T = (int(o.dims[i]) for i in (1, 2, 3, 4, 5, 6))
+        a = self.get(o.off[0], M * K, 1).reshape(M, K)
+        bt = self.get(o.off[1], N * K, 1).reshape(N, K)
+        acc = a @ bt.T
+        bias = self.get(o.off[4], N, 4) if o.flags & C.F_BIAS else None
+        v = np.empty_like(acc)
+        for c in range(N // Cw):
+            m, s = int(o.aux[c]) >> 8, int(o.aux[c]) & 255
+            cols = slice(c * Cw, (c + 1) * Cw)
+            add = bias[cols] if bias is not None else _rnd(s)
+            v[:, cols] = np.clip((acc[:, cols] * m + add) >> s, -128, 127)
+        mem, base = self._mem(o.off[2])
+        ors = int(o.strides[3])
+        for r in range(M):
+            mem[base + r * ors: base + r * ors + R] = v[r, :R].astype(np.int8).view(np.uint8)
+        if R < N:
+            N2 = N - R
+            mem2, base2 = self._mem(o.off[6])
+            r = np.arange(M)[:, None]
+            idx = (r // T) * (N2 * T) + np.arange(N2)[None, :] * T + r % T
+            flat = mem2[base2:].view(np.int8)
+            assert idx.max() < flat.size, "write outside region"
+            flat[idx] = v[:, R:].astype(np.int8)
 
     def k2(self, o):                                    # LUT
         n = int(o.dims[0])

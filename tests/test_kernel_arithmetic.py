@@ -9,9 +9,6 @@ against the plain definitions (CPU). Each test names the kernel code that uses t
   32 multiply and a shift.
 - ceil_pow2_div (attention.cuh): ceil(2^(31 + lg) / S) from a correctly rounded double quotient and two exact
   64-bit checks; and the pass-B division floor(n / S) = umulhi(n, m) >> (lg - 1) it feeds.
-- the wide requant (rowops.cuh norm_row_kernel, attention.cuh scores, gemm.cuh epilogue): with 1 <= s <= 32 and
-  0 <= M < 2^(s-1) (any M when s = 32), the high word of the 64-bit a * (M 2^(32-s)) + c 2^(32-s) + b 2^32 is
-  ((a M + c) >> s) + b for every int32 a and c = 2^(s-1) (b = 0 in the GEMM and the scores).
 """
 import random
 
@@ -104,22 +101,3 @@ def test_ceil_pow2_div_equals_the_exact_ceiling_and_divides_exactly():
             if 0 <= n < 2 ** 31:
                 assert ((n * m) >> 32) >> (lg - 1) == n // S, (n, S)
 
-
-def _wide_ok(s, m):
-    return 1 <= s <= 32 and m >= 0 and (s == 32 or m < (1 << (s - 1)))
-
-
-def test_wide_requant_equals_multiply_add_shift():
-    rng = random.Random(5)
-    for _ in range(40000):
-        s = rng.randrange(1, 33)
-        m = rng.randrange(0, 1 << min(31, s - 1)) if s < 32 else rng.randrange(0, 1 << 31)
-        assert _wide_ok(s, m)
-        a = rng.randrange(-(1 << 31), 1 << 31)
-        b = rng.randrange(-128, 128)
-        c = (1 << (s - 1)) + (rng.randrange(-(1 << 20), 1 << 20) * m if rng.random() < 0.5 else 0)
-        mw = m << (32 - s)
-        assert mw < (1 << 31)
-        hi = (a * mw + (c << (32 - s)) + (b << 32)) >> 32          # Python ints: exact, floor shifts
-        assert hi == ((a * m + c) >> s) + b, (a, m, s, b, c)
-    assert not _wide_ok(0, 0) and not _wide_ok(5, 16) and _wide_ok(5, 15) and _wide_ok(32, (1 << 31) - 1)

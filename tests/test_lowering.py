@@ -63,6 +63,25 @@ def test_nanogpt_block_lowering_fuses_and_matches():
     _check(run_program(cm, {"x": xq}), want.values, cm.outputs)
 
 
+def test_qkv_projections_lower_to_one_split_gemm():
+    """The q, k, v linears of a block whose width is whole 256-column tiles become one split-output GEMM (q and k
+    side by side, v transposed for the attention), and the emulated launch list still equals the oracle."""
+    from anvil import workloads as W
+    from anvil.runtime import cuda as C
+    cfg = W.GPTConfig(vocab_size=1, block_size=64, n_layer=1, n_head=4, n_embd=256)
+    mod = W.build_block(cfg, 12)
+    import torch
+    rng = np.random.default_rng(1)
+    cm = anvil.compile(mod, (torch.zeros(1, 64, 256),), [rng.standard_normal((4, 64, 256))])
+    prog = cm.program(2)
+    assert any(f.endswith(":qkv_split") for f in prog.fused)
+    splits = [o for o in prog.ops if o.kind == C.OP_GEMM and o.flags & C.F_SPLIT]
+    assert len(splits) == 1 and splits[0].dims[2] == 3 * 256 and splits[0].dims[5] == 2 * 256
+    xq = cm.quantize_input(rng.standard_normal((2, 64, 256)))
+    want = interp.run(cm.module, {"x": xq}, cm.consts, batch=True)
+    _check(run_program(cm, {"x": xq}), want.values, cm.outputs)
+
+
 def test_plan_reuses_and_never_overlaps_live_buffers():
     m, c, x, _ = random_case(3, batch=4)
     cm = anvil.compile(m, consts=c, prove=False)
