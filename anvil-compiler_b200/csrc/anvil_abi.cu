@@ -480,16 +480,19 @@ static int prepare_gemm(anvil_model *m, Launch &L) {
   if ((op.flags & ANVIL_F_LUT) && op.out_bytes != 1)
     return fail(ANVIL_E_BAD_ARG, "op %d: a LUT epilogue needs an i8 result", op.op_index);
   const int64_t o_grp = op.strides[4], o_gs = op.strides[5], o_cs = op.strides[6] ? op.strides[6] : 1;
-  if (a_bs < 0 || bt_bs < 0 || o_bs < 0 || o_rs < 0 || o_grp < 0 || o_gs < 0 || o_cs < 1 ||
-      (o_cs == 1 && o_rs < N))
+  const bool split = (op.flags & ANVIL_F_SPLIT) != 0;
+  const int64_t ncols = split ? op.dims[5] : N;        // columns that go to OUT (the rest of a split to off[6])
+  if (a_bs < 0 || bt_bs < 0 || o_bs < 0 || o_rs < 0 || o_grp < 0 || o_gs < 0 || o_cs < 1 || ncols < 0 ||
+      ncols > N || (o_cs == 1 && o_rs < ncols))
     return fail(ANVIL_E_BAD_ARG, "op %d: bad gemm strides", op.op_index);
   int rc;
   const uint64_t a_bytes = (uint64_t)((batch - 1) * a_bs + M * K);
   const uint64_t b_bytes = (uint64_t)((bt_bs ? (batch - 1) * bt_bs : 0) + N * K);
   const int64_t R = o_grp ? o_grp : M;
   const int64_t last_row = M - 1;
-  const uint64_t o_bytes = (uint64_t)(((batch - 1) * o_bs + (last_row / R) * o_gs + std::min<int64_t>(R - 1, last_row) * o_rs +
-                                       (N - 1) * o_cs + 1) * op.out_bytes);
+  const uint64_t o_bytes = ncols == 0 ? 0 : (uint64_t)(((batch - 1) * o_bs + (last_row / R) * o_gs +
+                                                        std::min<int64_t>(R - 1, last_row) * o_rs +
+                                                        (ncols - 1) * o_cs + 1) * op.out_bytes);
   if ((rc = resolve(m, op, 0, a_bytes, &L.ptr[0]))) return rc;
   if ((rc = resolve(m, op, 1, b_bytes, &L.ptr[1]))) return rc;
   if ((rc = resolve(m, op, 2, o_bytes, &L.ptr[2]))) return rc;
@@ -800,14 +803,16 @@ static int launch_op(anvil_model *m, Launch &L) {
           // one resident wave: every warp then walks several rows with the next row's load in flight
 #define NR_LAUNCH(NV8)                                                                                            \
   do {                                                                                                            \
-    static int per_sm = 0;                                                                                        \
-    if (!per_sm && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, norm_row_kernel<NV8>, 256, 0) != cudaSuccess) \
+    auto kern = bias ? norm_row_kernel<NV8, true> : norm_row_kernel<NV8, false>;                                  \
+    int per_sm = 0;                                                                                               \
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0) != cudaSuccess) {                    \
+      cudaGetLastError();                                                                                         \
       per_sm = 1;                                                                                                 \
+    }                                                                                                             \
     const int g = grid_for(m, op.dims[0], 8, std::max(1, per_sm));                                                \
-    norm_row_kernel<NV8><<<g, 256, 0, st>>>((const int8_t *)L.ptr[0], (const int8_t *)L.ptr[1],                   \
-                                            (const int32_t *)L.ptr[2], bias, (int8_t *)L.ptr[3], op.dims[0],       \
-                                            (int)op.dims[2], (int)op.mult, (int)op.shift, (int)op.ss_shift,       \
-                                            (int)op.ss_init, (op.flags & ANVIL_F_CENTER) ? 1 : 0);                \
+    kern<<<g, 256, 0, st>>>((const int8_t *)L.ptr[0], (const int8_t *)L.ptr[1], (const int32_t *)L.ptr[2], bias,  \
+                            (int8_t *)L.ptr[3], op.dims[0], (int)op.dims[2], (int)op.mult, (int)op.shift,         \
+                            (int)op.ss_shift, (int)op.ss_init, (op.flags & ANVIL_F_CENTER) ? 1 : 0);              \
   } while (0)
           switch (dd / 256) {
             case 1: NR_LAUNCH(1); break;

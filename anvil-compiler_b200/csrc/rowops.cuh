@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(256) norm_vec_kernel(const int8_t *__restrict_
 // Each output element takes one byte permute ({x_q, -mean} as 16-bit halves) and one dp2a for (x_q - mean) * w_q;
 // that times r * M is equal mod 2^32 to ((x - mean) * w * r) * M, exact because the proof bounds the true value.
 // The launch bounds keep the register budget that gives 5/4/3/2 resident blocks for 256/512/768/1024-wide rows.
-template <int NV8>
+template <int NV8, bool BIAS>
 __global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 3 : NV8 == 4 ? 2 : 1)
     norm_row_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w,
                                                        const int32_t *__restrict__ lut,
@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 
 #pragma unroll
   for (int v = 0; v < NV8; ++v) {
     const uint2 w2 = reinterpret_cast<const uint2 *>(w)[lane + 32 * v];
-    const uint2 b2 = bias ? reinterpret_cast<const uint2 *>(bias)[lane + 32 * v] : make_uint2(0, 0);
+    const uint2 b2 = BIAS ? reinterpret_cast<const uint2 *>(bias)[lane + 32 * v] : make_uint2(0, 0);
 #pragma unroll
     for (int q = 0; q < 8; ++q) br[8 * v + q] = sbyte_prmt(q < 4 ? b2.x : b2.y, q & 3);
 #pragma unroll
@@ -352,7 +352,8 @@ __global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 
         asm("prmt.b32 %0, %1, %2, %3;" : "=r"(a) : "r"(q < 4 ? xv[v].x : xv[v].y), "r"(nm),
             "r"((uint32_t)(q & 3) | (uint32_t)((q & 3) | 8) << 4 | 0x7600u));
         const int t = (q & 1) ? __dp2a_hi(a, (int)wp[4 * v + q / 2], 0) : __dp2a_lo(a, (int)wp[4 * v + q / 2], 0);
-        y[q] = (mad_wrap(t, rm, rnd) >> sh) + br[8 * v + q];
+        y[q] = mad_wrap(t, rm, rnd) >> sh;
+        if (BIAS) y[q] += br[8 * v + q];
       }
       orow[32 * v] = make_uint2(pack4_sat_s8(y[0], y[1], y[2], y[3]), pack4_sat_s8(y[4], y[5], y[6], y[7]));
     }

@@ -362,6 +362,7 @@ def run_ours(args):
     e2e_s = statistics.mean(e2e_times[args.warmup:])
     e2e_s = _max_over_ranks(dist, e2e_s, f"cuda:{local}")
     out_bytes = sum(np.asarray(res.ints[s]).nbytes for s in cm.outputs)
+    strong = _strong_scaling(cm, dm, xin, batch, c.seq, ws, dist, local, args) if ws > 1 else None
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8/int32", "data": "synthetic",
@@ -379,6 +380,8 @@ def run_ours(args):
             "launch_us": [[d.label, C.KIND_NAMES[d.kind], round(u, 2)] for d, u in zip(prog.devops, kus)],
             "gpu_launches": sum(1 for d in prog.devops if d.kind != C.OP_COPY) * args.steps,
             "clocks": clk.summary()}
+    if strong is not None:
+        line["strong_scaling"] = strong
     if rank == 0 and ws == 1 and not args.no_sweep:
         line["gemm_sweep_c4"] = gemm_sweep(i8peak or 2 * bf16)
     if rank == 0 and ws == 1 and not args.no_cpu:
@@ -389,6 +392,28 @@ def run_ours(args):
     if dist is not None:
         dist.destroy_process_group()
     return 0
+
+
+def _strong_scaling(cm, dm, xin, global_batch, seq, ws, dist, local, args):
+    """The config's stated batch as one fixed global batch split across the ws ranks (ceil(B / ws) sequences per
+    rank, contiguous shards as CudaParams(devices=...) splits them): device-timed graph replays of each rank's
+    shard, max over ranks, whole-job tokens/s."""
+    import torch
+    per = -(-global_batch // ws)
+    prog = cm.program(per)
+    dm.prepare(prog.ops, prog.plan.arena, key=(per, "outputs", False))
+    rank = int(os.environ.get("RANK", "0"))
+    lo = min(rank * per, global_batch - per)
+    dm.write(prog.inputs[cm.inputs[0]][0], np.ascontiguousarray(xin[lo:lo + per]))
+    dm.run_device(max(1, args.warmup), use_graph=True)
+    torch.cuda.synchronize()
+    _barrier(dist, local)
+    ms = dm.run_device(args.steps, use_graph=True)
+    torch.cuda.synchronize()
+    _barrier(dist, local)
+    ms = _max_over_ranks(dist, ms, f"cuda:{local}") / args.steps
+    return {"global_batch": global_batch, "batch_per_gpu": per, "ms_per_step": ms,
+            "value": global_batch * seq / (ms / 1000.0), "unit": "tokens/s", "scaling": "strong"}
 
 
 def _gate(cm, prog, dm, sample, want, when):
