@@ -584,7 +584,8 @@ class Lowering:
                 return False
         dims = [g.qt(o.b).dims for o in group]
         K, C = dims[0]
-        return all(d == (K, C) for d in dims) and C % 256 == 0 and K % 16 == 0
+        # the transposed part leaves through 32-row tile stores inside one sequence: T a multiple of 32
+        return all(d == (K, C) for d in dims) and C % 256 == 0 and K % 16 == 0 and self.vt_gemm[id(v)] % 32 == 0
 
     # ---- memory-bound ops
     def _act(self, value, label):
