@@ -619,6 +619,18 @@ static int prepare_attention(anvil_model *m, Launch &L) {
   a.op_index = op.op_index;
   div_magic((int64_t)B * H, &a.bh_magic, &a.bh_shift);
   div_magic(H, &a.h_magic, &a.h_shift);
+  // blocks of about two rounds of items: hb * nqt close to 2 x the CTAs, at most every (batch, head) pair
+  {
+    const int64_t grid = std::min<int64_t>((int64_t)B * H * a.nqt, m->sms);
+    int64_t hb = std::max<int64_t>(1, (2 * grid + a.nqt / 2) / a.nqt);
+    hb = std::min<int64_t>(hb, (int64_t)B * H);
+    const int64_t last = (int64_t)B * H - ((int64_t)B * H - 1) / hb * hb;
+    a.hb = (int)hb;
+    a.hb_last = (int)last;
+    div_magic(hb * a.nqt, &a.blk_magic, &a.blk_shift);
+    div_magic(hb, &a.hb_magic, &a.hb_shift);
+    div_magic(last, &a.last_magic, &a.last_shift);
+  }
   L.hd = (int)HD;
   return ANVIL_OK;
 }

@@ -39,6 +39,11 @@ struct AttnParams {
   int op_index;
   uint32_t bh_magic, h_magic;          // tile_div by B*H and by H (work-item decode)
   int bh_shift, h_shift;
+  // work items come in blocks of hb (batch, head) pairs x nqt query tiles: tile_div by hb * nqt, by hb and by the
+  // head count of the last, partial block (hb_last)
+  int hb, hb_last;
+  uint32_t blk_magic, hb_magic, last_magic;
+  int blk_shift, hb_shift, last_shift;
 };
 
 template <int HD>
@@ -96,23 +101,41 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
 }
 
 
+// Entry x of this lane's copy of the replicated exp LUT, whose entry 0 sits at shared address `base` (entries
+// COPIES words apart): one shift-add and one 32-bit shared load. The table does not change while the softmax passes
+// read it (it is written once, before the block-wide barrier that starts the kernel), so the load needs no ordering.
+template <int COPIES>
+__device__ __forceinline__ int lut_at(uint32_t base, int x) {
+  int v;
+  asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(base + (uint32_t)(x * (4 * COPIES))));
+  return v;
+}
+
 // byte offset of 16-byte chunk `ch` (0..7) of row `r` (0..127) inside one 128 x 128 P slab (SW128 K-major)
 __device__ __forceinline__ int pslab_off(int r, int ch) { return (r >> 3) * 1024 + (r & 7) * 128 + ((ch ^ (r & 7)) << 4); }
 
 constexpr int ATTN_SOFTMAX_THREADS = 512;                 // 16 warps: 4 threads per query row
 constexpr int ATTN_THREADS = 64 + ATTN_SOFTMAX_THREADS + 32;   // + warp 18, the V^T producer
 
-// One work item: (batch, head) and a 128-query tile, heaviest causal tiles first.
+// One work item: (batch, head) and a 128-query tile. Items come in blocks of hb (batch, head) pairs (the last
+// block may hold fewer); inside a block the query tiles go heaviest causal tile first, the pairs fastest. A
+// block's items run within a few rounds of the persistent CTAs, so the K tiles and V^T slabs its pairs share are
+// read from HBM once and then from L2, while the CTAs of one round still see tiles of equal or neighbouring weight.
 struct AttnTile {
   int b, h, bh, q0, nkv;
 };
 
 __device__ __forceinline__ AttnTile attn_tile(const AttnParams &p, int t) {
-  const uint32_t BH = (uint32_t)(p.B * p.H);
   AttnTile w;
-  const uint32_t r = tile_div((uint32_t)t, BH, p.bh_magic, p.bh_shift);
+  const uint32_t per_blk = (uint32_t)(p.hb * p.nqt);
+  const uint32_t blk = tile_div((uint32_t)t, per_blk, p.blk_magic, p.blk_shift);
+  const uint32_t wi = (uint32_t)t - blk * per_blk;
+  const int base = (int)blk * p.hb;
+  const bool last = base + p.hb > p.B * p.H;
+  const uint32_t heads = last ? (uint32_t)p.hb_last : (uint32_t)p.hb;
+  const uint32_t r = last ? tile_div(wi, heads, p.last_magic, p.last_shift) : tile_div(wi, heads, p.hb_magic, p.hb_shift);
   const int qt = p.nqt - 1 - (int)r;
-  w.bh = (int)((uint32_t)t - r * BH);
+  w.bh = base + (int)(wi - r * heads);
   w.b = (int)tile_div((uint32_t)w.bh, (uint32_t)p.H, p.h_magic, p.h_shift);
   w.h = w.bh - w.b * p.H;
   w.q0 = qt * 128;
@@ -323,7 +346,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     const int opart = part - (4 - HD / 32);
     auto o_epilogue = [&](const AttnTile &w, int k) {
       const int row = w.q0 + r;
-      if (opart >= 0 && __all_sync(0xffffffffu, mbar_wait(ofull, k & 1, abort, p.flags, p.op_index))) {
+      if (opart >= 0 && __all_sync(0xffffffffu, mbar_wait_idle(ofull, k & 1, abort, p.flags, p.op_index))) {
         tc_fence_after();
         int32_t acc[32];
         tmem_ld32(tmem + ((uint32_t)lane_base << 16) + (uint32_t)(Cfg::O_COL + opart * 32), acc);
@@ -363,7 +386,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       bool ok = true;
       for (int j = 0; j < w.nkv; ++j, ++gs) {
         const int sb = gs % Cfg::NSB;
-        ok = __all_sync(0xffffffffu, mbar_wait(&sfull[sb], (gs / Cfg::NSB) & 1, abort, p.flags, p.op_index));
+        ok = __all_sync(0xffffffffu, mbar_wait_idle(&sfull[sb], (gs / Cfg::NSB) & 1, abort, p.flags, p.op_index));
         if (!ok) break;                     // warp-uniform: the TMEM load below is .sync.aligned
         tc_fence_after();
         int32_t acc[32];
@@ -386,7 +409,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
 #pragma unroll
         for (int q = 0; q < 8; ++q) wq[q] = pack4_sat_s8(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         // P slab j still feeds the previous tile's P V MMA until pfree[j] completes
-        ok = __all_sync(0xffffffffu, mbar_wait(&pfree[j], ((fph >> j) & 1u) ^ 1u, abort, p.flags, p.op_index));
+        ok = __all_sync(0xffffffffu, mbar_wait_idle(&pfree[j], ((fph >> j) & 1u) ^ 1u, abort, p.flags, p.op_index));
         fph ^= 1u << j;
         if (!ok) break;
         uint8_t *slab = pbuf + j * Cfg::P_SLAB;
@@ -413,9 +436,9 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           : "memory");
       if (stop) { stopped = true; break; }
       mx = max(max(red_max[r], red_max[128 + r]), max(red_max[256 + r], red_max[384 + r]));
-      // a kept score x <= mx (a signed byte of the slab) has lut[x - mx + 255] at lutc[x * COPIES] in this lane's
+      // a kept score x <= mx (a signed byte of the slab) has lut[x - mx + 255] at lut_at(lutc, x) in this lane's
       // copy; a masked column's byte may exceed mx and is clamped to it first, so every index is in [0, 255]
-      const int32_t *lutc = lut + (255 - mx) * Cfg::LUT_COPIES + lcopy;
+      const uint32_t lutc = smem_u32(lut + (255 - mx) * Cfg::LUT_COPIES + lcopy);
       // pass A: partial S = sum over this part's kept columns of lut[x - max + 255]
       int tot0 = 0, tot1 = 0;
       for (int j = 0; j < w.nkv && ok; ++j) {
@@ -429,13 +452,13 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           // two independent three-input adds per word (each folds two entries into one accumulator)
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            tot0 += lutc[sbyte_prmt(wv[q], 0) * Cfg::LUT_COPIES] + lutc[sbyte_prmt(wv[q], 1) * Cfg::LUT_COPIES];
-            tot1 += lutc[sbyte_prmt(wv[q], 2) * Cfg::LUT_COPIES] + lutc[sbyte_prmt(wv[q], 3) * Cfg::LUT_COPIES];
+            tot0 += lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q], 0)) + lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q], 1));
+            tot1 += lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q], 2)) + lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q], 3));
           }
         } else {
 #pragma unroll
           for (int q = 0; q < 32; ++q) {
-            const int e = lutc[min(sbyte_prmt(wv[q >> 2], q & 3), mx) * Cfg::LUT_COPIES];
+            const int e = lut_at<Cfg::LUT_COPIES>(lutc, min(sbyte_prmt(wv[q >> 2], q & 3), mx));
             tot0 += cb + q < kept ? e : 0;
           }
         }
@@ -467,14 +490,14 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           if (__all_sync(0xffffffffu, cb + 32 <= kept)) {
 #pragma unroll
             for (int q = 0; q < 32; ++q) {
-              const unsigned num = (unsigned)lutc[sbyte_prmt(wv[q >> 2], q & 3) * Cfg::LUT_COPIES] * one2 + half2;
+              const unsigned num = (unsigned)lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q >> 2], q & 3)) * one2 + half2;
               pv[q] = (int)(__umulhi(num, magic) >> msh);
             }
           } else {
 #pragma unroll
             for (int q = 0; q < 32; ++q) {
               const int x = min(sbyte_prmt(wv[q >> 2], q & 3), mx);
-              const unsigned num = (unsigned)lutc[x * Cfg::LUT_COPIES] * one2 + half2;
+              const unsigned num = (unsigned)lut_at<Cfg::LUT_COPIES>(lutc, x) * one2 + half2;
               pv[q] = cb + q < kept ? (int)(__umulhi(num, magic) >> msh) : 0;
             }
           }

@@ -270,9 +270,10 @@ __global__ void __launch_bounds__(256) norm_vec_kernel(const int8_t *__restrict_
 // per-element shift (c == 0) the centered sum of squares is sum(x^2) - 2 mean sum(x) + d mean^2, the same integer.
 // Each output element takes one byte permute ({x_q, -mean} as 16-bit halves) and one dp2a for (x_q - mean) * w_q;
 // that times r * M is equal mod 2^32 to ((x - mean) * w * r) * M, exact because the proof bounds the true value.
-// The launch bounds keep the register budget that gives 5/4/3/2 resident blocks for 256/512/768/1024-wide rows.
+// The launch bounds keep the register budget that gives 5/4/3 (4 without a bias)/2 resident blocks for
+// 256/512/768/1024-wide rows.
 template <int NV8, bool BIAS>
-__global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 3 : NV8 == 4 ? 2 : 1)
+__global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? (BIAS ? 3 : 4) : NV8 == 4 ? 2 : 1)
     norm_row_kernel(const int8_t *__restrict__ x, const int8_t *__restrict__ w,
                                                        const int32_t *__restrict__ lut,
                                                        const int8_t *__restrict__ bias, int8_t *__restrict__ out,

@@ -279,7 +279,11 @@ def run_ours(args):
     ws, rank, local = _dist()
     if ws > 1:
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")    # stdout carries only the JSON line
+        # NCCL's communicator set-up lines (one per rank: rank, device, bus id) go to stderr; stdout carries only
+        # the JSON line
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     torch.cuda.set_device(local)
     dist = _pg(ws, "nccl")
     cfg = args.config

@@ -101,3 +101,39 @@ def test_ceil_pow2_div_equals_the_exact_ceiling_and_divides_exactly():
             if 0 <= n < 2 ** 31:
                 assert ((n * m) >> 32) >> (lg - 1) == n // S, (n, S)
 
+
+
+def _div_magic(d):
+    if d <= 1:
+        return 0, 0
+    l = (d - 1).bit_length()
+    return ((1 << (31 + l)) + d - 1) // d, l - 1
+
+
+def _tile_div(x, d, m, s):
+    return x if d == 1 else (x * m >> 32) >> s
+
+
+def test_attention_work_blocks_cover_every_item_once():
+    """attn_tile (attention.cuh) with the host's block size (anvil_abi.cu prepare_attention): the items
+    0 .. B*H*nqt - 1 map one to one onto (batch-head, query tile) pairs, heaviest tile first inside each block of
+    hb pairs, for full and partial last blocks."""
+    for BH, nqt, sms in [(768, 8, 148), (24, 8, 148), (5, 3, 148), (64, 1, 148), (37, 8, 148), (1, 1, 148)]:
+        grid = min(BH * nqt, sms)
+        hb = min(max(1, (2 * grid + nqt // 2) // nqt), BH)
+        last = BH - (BH - 1) // hb * hb
+        bm, bs = _div_magic(hb * nqt)
+        hm, hs = _div_magic(hb)
+        lm, ls = _div_magic(last)
+        seen = set()
+        for t in range(BH * nqt):
+            blk = _tile_div(t, hb * nqt, bm, bs)
+            wi = t - blk * hb * nqt
+            base = blk * hb
+            heads = last if base + hb > BH else hb
+            r = _tile_div(wi, heads, lm, ls) if base + hb > BH else _tile_div(wi, heads, hm, hs)
+            assert r == wi // heads
+            bh, qt = base + wi - r * heads, nqt - 1 - r
+            assert 0 <= bh < BH and 0 <= qt < nqt
+            seen.add((bh, qt))
+        assert len(seen) == BH * nqt
