@@ -631,7 +631,6 @@ static int prepare_attention(anvil_model *m, Launch &L) {
     div_magic(hb, &a.hb_magic, &a.hb_shift);
     div_magic(last, &a.last_magic, &a.last_shift);
   }
-  a.lut_stride = 4 * (HD == 64 ? AttnCfg<64>::LUT_COPIES : AttnCfg<128>::LUT_COPIES);
   L.hd = (int)HD;
   return ANVIL_OK;
 }

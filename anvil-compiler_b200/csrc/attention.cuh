@@ -42,7 +42,6 @@ struct AttnParams {
   // work items come in blocks of hb (batch, head) pairs x nqt query tiles: tile_div by hb * nqt, by hb and by the
   // head count of the last, partial block (hb_last)
   int hb, hb_last;
-  int lut_stride;                      // bytes between consecutive exp-LUT entries (4 x the per-lane copies)
   uint32_t blk_magic, hb_magic, last_magic;
   int blk_shift, hb_shift, last_shift;
 };
@@ -111,20 +110,6 @@ __device__ __forceinline__ int lut_at(uint32_t base, int x) {
   asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(base + (uint32_t)(x * (4 * COPIES))));
   return v;
 }
-
-// The same load with the entry stride as a run-time value: the address then comes from one integer multiply-add
-// on the FMA pipe (a constant power-of-two stride becomes a shift-add on the ALU pipe, which the softmax passes
-// saturate first).
-__device__ __forceinline__ int lut_at_rt(uint32_t base, int x, uint32_t stride) {
-  uint32_t a;
-  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(a) : "r"((uint32_t)x), "r"(stride), "r"(base));
-  int v;
-  asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-  return v;
-}
-
-// floor(x / 2^s) for 2 <= s <= 31 as the high word of x * 2^(32 - s) (f = 2^(32 - s) <= 2^30): on the FMA pipe
-__device__ __forceinline__ int shr_hi(int x, int f) { return __mulhi(x, f); }
 
 // byte offset of 16-byte chunk `ch` (0..7) of row `r` (0..127) inside one 128 x 128 P slab (SW128 K-major)
 __device__ __forceinline__ int pslab_off(int r, int ch) { return (r >> 3) * 1024 + (r & 7) * 128 + ((ch ^ (r & 7)) << 4); }
@@ -347,7 +332,6 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     const int r = lane_base + lane;
     const int m1 = (int)p.m1;
     const int rnd1 = (int)round_term(p.s1);
-    const int f1 = p.s1 >= 2 ? 1 << (32 - p.s1) : 0;
     int32_t *red_max = reinterpret_cast<int32_t *>(smem + Cfg::OFF_RED);   // [4][128] partial row max
     int32_t *red_sum = red_max + 512;                                          // [4][128] partial row sum
     const int lcopy = lane % Cfg::LUT_COPIES;
@@ -413,14 +397,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         // saturating pack.
         int v[32];
 #pragma unroll
-        for (int q = 0; q < 32; ++q) v[q] = mad_wrap(acc[q], m1, rnd1);
-        if (f1) {                           // the shift as a high multiply (FMA pipe) when 2 <= s1
-#pragma unroll
-          for (int q = 0; q < 32; ++q) v[q] = shr_hi(v[q], f1);
-        } else {
-#pragma unroll
-          for (int q = 0; q < 32; ++q) v[q] >>= p.s1;
-        }
+        for (int q = 0; q < 32; ++q) v[q] = mad_wrap(acc[q], m1, rnd1) >> p.s1;
         if (__all_sync(0xffffffffu, cb + 32 <= kept)) {
 #pragma unroll
           for (int q = 0; q < 32; ++q) mx = max(mx, v[q]);
@@ -462,7 +439,6 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       // a kept score x <= mx (a signed byte of the slab) has lut[x - mx + 255] at lut_at(lutc, x) in this lane's
       // copy; a masked column's byte may exceed mx and is clamped to it first, so every index is in [0, 255]
       const uint32_t lutc = smem_u32(lut + (255 - mx) * Cfg::LUT_COPIES + lcopy);
-      const uint32_t lstride = (uint32_t)p.lut_stride;
       // pass A: partial S = sum over this part's kept columns of lut[x - max + 255]
       int tot0 = 0, tot1 = 0;
       for (int j = 0; j < w.nkv && ok; ++j) {
@@ -476,13 +452,13 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           // two independent three-input adds per word (each folds two entries into one accumulator)
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            tot0 += lut_at_rt(lutc, sbyte_prmt(wv[q], 0), lstride) + lut_at_rt(lutc, sbyte_prmt(wv[q], 1), lstride);
-            tot1 += lut_at_rt(lutc, sbyte_prmt(wv[q], 2), lstride) + lut_at_rt(lutc, sbyte_prmt(wv[q], 3), lstride);
+            tot0 += lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q], 0)) + lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q], 1));
+            tot1 += lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q], 2)) + lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q], 3));
           }
         } else {
 #pragma unroll
           for (int q = 0; q < 32; ++q) {
-            const int e = lut_at_rt(lutc, min(sbyte_prmt(wv[q >> 2], q & 3), mx), lstride);
+            const int e = lut_at<Cfg::LUT_COPIES>(lutc, min(sbyte_prmt(wv[q >> 2], q & 3), mx));
             tot0 += cb + q < kept ? e : 0;
           }
         }
@@ -502,10 +478,6 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       const int msh = lg > 0 ? lg - 1 : 0;
       const unsigned one2 = S > 1 ? (unsigned)p.one : 2u * (unsigned)p.one;
       const unsigned half2 = S > 1 ? (unsigned)(tot >> 1) : 2u * (unsigned)(tot >> 1);
-      // with msh >= 1 (S > 2) the final shift is a second high multiply, by 2^(32 - msh) (FMA pipe, not ALU);
-      // a warp with a row of S <= 2 (a degenerate exp LUT) keeps the shift
-      const unsigned fB = msh >= 1 ? 1u << (32 - msh) : 0u;
-      const bool hiB = __all_sync(0xffffffffu, S > 2);
       for (int j = 0; j < w.nkv && ok; ++j) {
         uint8_t *slab = pbuf + j * Cfg::P_SLAB;
         const int cb = j * 128 + part * 32;
@@ -516,24 +488,16 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           const uint32_t wv[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
           int pv[32];
           if (__all_sync(0xffffffffu, cb + 32 <= kept)) {
-            if (hiB) {
 #pragma unroll
-              for (int q = 0; q < 32; ++q) {
-                const unsigned num = (unsigned)lut_at_rt(lutc, sbyte_prmt(wv[q >> 2], q & 3), lstride) * one2 + half2;
-                pv[q] = (int)__umulhi(__umulhi(num, magic), fB);
-              }
-            } else {
-#pragma unroll
-              for (int q = 0; q < 32; ++q) {
-                const unsigned num = (unsigned)lut_at_rt(lutc, sbyte_prmt(wv[q >> 2], q & 3), lstride) * one2 + half2;
-                pv[q] = (int)(__umulhi(num, magic) >> msh);
-              }
+            for (int q = 0; q < 32; ++q) {
+              const unsigned num = (unsigned)lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q >> 2], q & 3)) * one2 + half2;
+              pv[q] = (int)(__umulhi(num, magic) >> msh);
             }
           } else {
 #pragma unroll
             for (int q = 0; q < 32; ++q) {
               const int x = min(sbyte_prmt(wv[q >> 2], q & 3), mx);
-              const unsigned num = (unsigned)lut_at_rt(lutc, x, lstride) * one2 + half2;
+              const unsigned num = (unsigned)lut_at<Cfg::LUT_COPIES>(lutc, x) * one2 + half2;
               pv[q] = cb + q < kept ? (int)(__umulhi(num, magic) >> msh) : 0;
             }
           }

@@ -138,20 +138,3 @@ def test_attention_work_blocks_cover_every_item_once():
             seen.add((bh, qt))
         assert len(seen) == BH * nqt
 
-
-def test_shift_as_high_multiply():
-    """attention.cuh shr_hi and the pass-B second stage: for 2 <= s <= 31 the high word of the signed 64-bit
-    x * 2^(32-s) is x >> s (arithmetic) for every int32 x, and for 1 <= s <= 31 the high word of the unsigned
-    t * 2^(32-s) is t >> s for every uint32 t."""
-    rng = random.Random(9)
-    xs = [rng.randrange(-(1 << 31), 1 << 31) for _ in range(3000)] + [-(1 << 31), -1, 0, 1, (1 << 31) - 1]
-    for s in range(2, 32):
-        f = 1 << (32 - s)
-        assert f < (1 << 31)
-        for x in xs:
-            assert (x * f) >> 32 == x >> s
-    ts = [rng.randrange(0, 1 << 32) for _ in range(3000)] + [0, 1, (1 << 32) - 1]
-    for s in range(1, 32):
-        f = 1 << (32 - s)
-        for t in ts:
-            assert (t * f) >> 32 == t >> s
