@@ -29,7 +29,9 @@ from .ir import graph as g
 
 BACKENDS = ("cuda",)
 PIPELINE_MODELS = 4          # device models (arenas + streams) a pipelined run rotates over
-PIPELINE_TOKENS = 16384      # "auto" pipeline chunk size, in tokens
+PIPELINE_TOKENS = 8192       # "auto" pipeline chunk size, in tokens (c3 batch 64 on one B200, pinned buffers,
+                             # four device models: 8 chunks 1.43 ms per call, 4 chunks 1.53 ms, 16 chunks 1.78 ms;
+                             # 3, 6 or 8 models and tapered chunk sizes were slower)
 NOMINAL_PEAKS = {"int8_tops": 4500.0, "hbm_gbs": 7700.0}    # B200 dense int8 tensor and HBM3e, NVIDIA's figures
 GUARD_BYTES = 256            # canary bytes after every buffer of a guarded (stray-write checked) run
 
