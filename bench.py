@@ -277,13 +277,17 @@ def run_ours(args):
     from anvil.runtime import cuda as C
 
     ws, rank, local = _dist()
+    json_fd = 1
     if ws > 1:
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        # NCCL's communicator set-up lines (one per rank: rank, device, bus id) go to stderr; stdout carries only
-        # the JSON line
+        # NCCL's banner and communicator set-up lines (one per rank: rank, device, bus id) are printed to the
+        # process's stdout: point file descriptor 1 at stderr for everything the libraries print, and keep a copy
+        # of the real stdout for the one JSON line
         os.environ.setdefault("NCCL_DEBUG", "INFO")
         os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        sys.stdout.flush()
+        json_fd = os.dup(1)
+        os.dup2(2, 1)
     torch.cuda.set_device(local)
     dist = _pg(ws, "nccl")
     cfg = args.config
@@ -391,7 +395,8 @@ def run_ours(args):
     if rank == 0 and ws == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(cfg, cm, gen)
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        sys.stdout.flush()
+        os.write(json_fd, (json.dumps(line) + "\n").encode())
     dm.close()
     if dist is not None:
         dist.destroy_process_group()
