@@ -111,6 +111,25 @@ __device__ __forceinline__ int lut_at(uint32_t base, int x) {
   return v;
 }
 
+// Entry x of that copy where x is signed byte Q of the word w: one dp4a forms the address base + x * 4 * COPIES
+// (w's bytes signed, the selector's unsigned, only byte Q of it non-zero), replacing a byte permute and a
+// shift-add on the ALU pipe, the softmax passes' busiest.
+template <int COPIES, int Q>
+__device__ __forceinline__ int lut_byte(uint32_t base, uint32_t w) {
+  static_assert(4 * COPIES <= 255, "the entry stride must fit the selector byte");
+  uint32_t a;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(a) : "r"(w), "n"((4u * COPIES) << (8 * Q)), "r"(base));
+  int v;
+  asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+
+template <int COPIES>
+__device__ __forceinline__ int lut_byte_q(uint32_t base, uint32_t w, int q) {
+  return q == 0 ? lut_byte<COPIES, 0>(base, w) : q == 1 ? lut_byte<COPIES, 1>(base, w)
+       : q == 2 ? lut_byte<COPIES, 2>(base, w) : lut_byte<COPIES, 3>(base, w);
+}
+
 // byte offset of 16-byte chunk `ch` (0..7) of row `r` (0..127) inside one 128 x 128 P slab (SW128 K-major)
 __device__ __forceinline__ int pslab_off(int r, int ch) { return (r >> 3) * 1024 + (r & 7) * 128 + ((ch ^ (r & 7)) << 4); }
 
@@ -452,8 +471,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           // two independent three-input adds per word (each folds two entries into one accumulator)
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            tot0 += lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q], 0)) + lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q], 1));
-            tot1 += lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q], 2)) + lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q], 3));
+            tot0 += lut_byte<Cfg::LUT_COPIES, 0>(lutc, wv[q]) + lut_byte<Cfg::LUT_COPIES, 1>(lutc, wv[q]);
+            tot1 += lut_byte<Cfg::LUT_COPIES, 2>(lutc, wv[q]) + lut_byte<Cfg::LUT_COPIES, 3>(lutc, wv[q]);
           }
         } else {
 #pragma unroll
@@ -490,7 +509,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           if (__all_sync(0xffffffffu, cb + 32 <= kept)) {
 #pragma unroll
             for (int q = 0; q < 32; ++q) {
-              const unsigned num = (unsigned)lut_at<Cfg::LUT_COPIES>(lutc, sbyte_prmt(wv[q >> 2], q & 3)) * one2 + half2;
+              const unsigned num = (unsigned)lut_byte_q<Cfg::LUT_COPIES>(lutc, wv[q >> 2], q & 3) * one2 + half2;
               pv[q] = (int)(__umulhi(num, magic) >> msh);
             }
           } else {

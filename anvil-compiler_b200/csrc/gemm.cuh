@@ -53,6 +53,19 @@ struct GemmParams {
   int smult[8], sshift[8];
 };
 
+// Entry e of a lane's LUT copy (entries 128 bytes apart from `base`) where e is unsigned byte k of w: one dp4a
+// forms the address base + 128 e (a byte permute and a shift-add otherwise).
+__device__ __forceinline__ int lut_ubyte(uint32_t base, uint32_t w, int k) {
+  uint32_t a;
+  if (k == 0) asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(a) : "r"(w), "n"(128u), "r"(base));
+  else if (k == 1) asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(a) : "r"(w), "n"(128u << 8), "r"(base));
+  else if (k == 2) asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(a) : "r"(w), "n"(128u << 16), "r"(base));
+  else asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(a) : "r"(w), "n"(128u << 24), "r"(base));
+  int v;
+  asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+
 // y -> the fused residual add's result (32-bit exact under the static int32 proof)
 template <int OB>
 __device__ __forceinline__ int residual_add(int y, int rv, const GemmParams &p) {
@@ -457,6 +470,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint32_t aphase = 0;
     constexpr int lo = OB == 1 ? -128 : -32768, hi = OB == 1 ? 127 : 32767;
     const int32_t *lt = p.lut ? lut_r + lane : nullptr;       // this lane's copy: lt[32 e] = lut[e]
+    const uint32_t lt_addr = smem_u32(lut_r + lane);            // its shared address: entry e at + 128 e
     // the requant constants (per tile for a split output, whose chunks have their own)
     int m32 = 0, sh = 0, rnd = 0;
     auto set_requant = [&](long long mult, int shift) {
@@ -573,7 +587,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               for (int q = 0; q < 4; ++q) {
                 const uint32_t w = pack4_sat_s8(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]) ^ 0x80808080u;
 #pragma unroll
-                for (int k = 0; k < 4; ++k) v[4 * q + k] = lt[ubyte(w, k) * 32];
+                for (int k = 0; k < 4; ++k) v[4 * q + k] = lut_ubyte(lt_addr, w, k);
               }
             } else {
 #pragma unroll

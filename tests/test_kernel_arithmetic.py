@@ -138,3 +138,27 @@ def test_attention_work_blocks_cover_every_item_once():
             seen.add((bh, qt))
         assert len(seen) == BH * nqt
 
+
+
+def _dp4a_s32_u32(a, b, c):
+    """PTX dp4a.s32.u32: the four bytes of a signed, of b unsigned, products summed into c (mod 2^32)."""
+    tot = c
+    for i in range(4):
+        x = (a >> (8 * i)) & 255
+        x = x - 256 if x >= 128 else x
+        tot += x * ((b >> (8 * i)) & 255)
+    return tot & 0xFFFFFFFF
+
+
+def test_lut_address_by_dp4a():
+    """attention.cuh lut_byte: dp4a.s32.u32(w, stride << 8q, base) is base + stride * (signed byte q of w), the
+    shared address of that byte's exp-LUT entry, for both entry strides the kernel uses (32 and 128 bytes)."""
+    rng = random.Random(11)
+    for stride in (32, 128):
+        for _ in range(2000):
+            w = rng.randrange(0, 1 << 32)
+            base = rng.randrange(16384, 1 << 18)
+            for q in range(4):
+                x = (w >> (8 * q)) & 255
+                x = x - 256 if x >= 128 else x
+                assert _dp4a_s32_u32(w, stride << (8 * q), base) == base + stride * x
