@@ -596,11 +596,13 @@ static int prepare_attention(anvil_model *m, Launch &L) {
   const CUtensorMapSwizzle qk_swz = HD == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   const uint64_t qdims[4] = {(uint64_t)HD, (uint64_t)H, (uint64_t)T1, (uint64_t)B};
   const uint64_t qstr[3] = {(uint64_t)st[1], (uint64_t)st[2], (uint64_t)(B > 1 ? st[0] : st[2] * T1)};
-  const uint32_t qbox[4] = {(uint32_t)HD, 1, 128, 1};
+  // Q tiles arrive as four 32-row blocks (the kernel places them in either order), K tiles as 128 keys
+  const uint32_t qbox[4] = {(uint32_t)HD, 1, 32, 1};
   if ((rc = make_map(&L.mapA, L.ptr[0], 4, qdims, qstr, qbox, qk_swz))) return rc;
   const uint64_t kdims[4] = {(uint64_t)HD, (uint64_t)H, (uint64_t)T2, (uint64_t)B};
   const uint64_t kstr[3] = {(uint64_t)st[4], (uint64_t)st[5], (uint64_t)(B > 1 ? st[3] : st[5] * T2)};
-  if ((rc = make_map(&L.mapB, L.ptr[1], 4, kdims, kstr, qbox, qk_swz))) return rc;
+  const uint32_t kbox[4] = {(uint32_t)HD, 1, 128, 1};
+  if ((rc = make_map(&L.mapB, L.ptr[1], 4, kdims, kstr, kbox, qk_swz))) return rc;
   const uint64_t vdims[2] = {(uint64_t)T2, (uint64_t)(B * H * HD)};
   const uint64_t vstr[1] = {(uint64_t)T2};
   const uint32_t vbox[2] = {128, (uint32_t)HD};

@@ -236,7 +236,11 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         const AttnTile w = attn_tile(p, t);
         if (!mbar_wait_idle(qempty, (k & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
         mbar_arrive_expect_tx(qfull, Cfg::Q_BYTES);
-        tma_load_4d(smem + Cfg::OFF_Q, &mapQ, 0, w.h, w.q0, w.b, qfull);
+        // query rows q0 + 32 b + i go to TMEM lane 32 (b ^ flip) + i (flip = 3 on odd items of this CTA)
+        const int flip = (k & 1) * 3;
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          tma_load_4d(smem + Cfg::OFF_Q + (b ^ flip) * (Cfg::Q_BYTES / 4), &mapQ, 0, w.h, w.q0 + 32 * b, w.b, qfull);
         for (int j = 0; j < w.nkv; ++j, ++gk) {
           const int st = gk % Cfg::KS;
           if (!mbar_wait_idle(&kempty[st], ((gk / Cfg::KS) & 1) ^ 1, abort, p.flags, p.op_index)) { ok = false; break; }
@@ -363,8 +367,15 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     // these are the warps with the least probability work. It runs after the next tile's score pass, by which
     // time the tile's P V MMAs are long done, so no warp waits on them at a tile boundary.
     const int opart = part - (4 - HD / 32);
+    // query row (within the tile) of this thread's TMEM lane on the CTA's k-th item: the Q producer reverses the
+    // order of the four 32-row blocks on odd items, so the row group holding the heaviest causal rows alternates
+    // between the SMSPs (a warp reads TMEM lanes 32 (warp % 4) + i only, and runs on SMSP warp % 4)
+    const auto qrow = [&](int k) { return 32 * ((warp & 3) ^ ((k & 1) * 3)) + lane; };
+    // the four warps of one row group (one per part) meet at named barrier 1 + (warp & 3); the row groups do not
+    // wait for one another
+    const int gbar = 1 + (warp & 3);
     auto o_epilogue = [&](const AttnTile &w, int k) {
-      const int row = w.q0 + r;
+      const int row = w.q0 + qrow(k);
       if (opart >= 0 && __all_sync(0xffffffffu, mbar_wait_idle(ofull, k & 1, abort, p.flags, p.op_index))) {
         tc_fence_after();
         int32_t acc[32];
@@ -396,7 +407,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     const int off0 = pslab_off(r, 2 * part), off1 = pslab_off(r, 2 * part + 1);
     for (int t; (t = attn_item(k, ntiles)) >= 0; ++k) {
       const AttnTile w = attn_tile(p, t);
-      const int row = w.q0 + r;
+      const int row = w.q0 + qrow(k);
       const int kept = p.causal ? min(row + 1, p.T2) : p.T2;
       // Every pass classifies this thread's 32 columns of slab j for the warp as a whole (votes, so the branches
       // are warp-uniform): all kept for every row of the warp (no mask), none kept (nothing to read), or the
@@ -442,16 +453,17 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       if (k > 0 && ok) o_epilogue(prev, k - 1);
       prev = w;
       red_max[part * 128 + r] = min(127, mx);
-      // every softmax warp takes the same decision to stop (the named barriers need all 16): the abort word is
-      // OR-reduced across the 512 threads by this barrier itself
+      // the four warps of the row group take the same decision to stop (their named barrier needs all four): the
+      // abort word is OR-reduced across the group's 128 threads by this barrier itself. Other groups see the abort
+      // word at their next barrier or bounded wait.
       int stop;
       asm volatile(
           "{\n\t.reg .pred P;\n\t"
           "setp.ne.s32 P, %1, 0;\n\t"
-          "bar.red.or.pred P, 1, 512, P;\n\t"
+          "bar.red.or.pred P, %2, 128, P;\n\t"
           "selp.s32 %0, 1, 0, P;\n\t}"
           : "=r"(stop)
-          : "r"(*abort)
+          : "r"(*abort), "r"(gbar)
           : "memory");
       if (stop) { stopped = true; break; }
       mx = max(max(red_max[r], red_max[128 + r]), max(red_max[256 + r], red_max[384 + r]));
@@ -483,7 +495,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         }
       }
       red_sum[part * 128 + r] = tot0 + tot1;
-      asm volatile("bar.sync 1, 512;" ::: "memory");
+      asm volatile("bar.sync %0, 128;" ::"r"(gbar) : "memory");
       const int tot = red_sum[r] + red_sum[128 + r] + red_sum[256 + r] + red_sum[384 + r];
       // pass B: p = floor((e*one + S/2) / S), masked entries 0. The division is a multiply by a per-row magic
       // number (Granlund & Montgomery, "Division by invariant integers using multiplication", 1994): with
