@@ -34,6 +34,7 @@ PIPELINE_TOKENS = 8192       # "auto" pipeline chunk size, in tokens (c3 batch 6
                              # 3, 6 or 8 models and tapered chunk sizes were slower)
 NOMINAL_PEAKS = {"int8_tops": 4500.0, "hbm_gbs": 7700.0}    # B200 dense int8 tensor and HBM3e, NVIDIA's figures
 GUARD_BYTES = 256            # canary bytes after every buffer of a guarded (stray-write checked) run
+MAX_OUTSTANDING = 32         # submit() calls queued at once (each holds one completion ticket per device model)
 
 
 @dataclass(frozen=True)
@@ -118,6 +119,67 @@ class CudaRunResult:
     kernel_us: dict = field(default_factory=dict)
 
 
+def _wait_tickets(tickets):
+    """Wait on every (DeviceModel, ticket); then raise the first device error among them (none is left pending)."""
+    errs = []
+    for dm, t in tickets:
+        try:
+            dm.wait_ticket(t)
+        except Exception as e:
+            errs.append(e)
+    if errs:
+        raise errs[0]
+
+
+class PendingRun:
+    """A run queued by CompiledModel.submit: its copies and kernels are on the device streams; wait() blocks until
+    they are done and returns the RunOutput that run() would have returned (or raises its error). The input and
+    output arrays must stay alive and unmodified until then (the object holds references to them)."""
+
+    def __init__(self, model, batch, batched, shards, tickets, keep):
+        self._model = model
+        self._batch, self._batched, self._shards = batch, batched, shards
+        self._tickets = tickets           # [(DeviceModel, ticket)]
+        self._keep = keep                 # (bound inputs, per-shard input copies, outputs)
+        self._result = None
+        self._error = None
+
+    def done(self) -> bool:
+        """True once wait() has collected the run (it never blocks)."""
+        return self._tickets is None
+
+    def _finish(self):
+        if self._tickets is None:
+            return
+        tickets, self._tickets = self._tickets, None
+        try:
+            _wait_tickets(tickets)
+        except Exception as e:
+            self._error = e
+        bound, _, ints = self._keep
+        self._keep = None
+        if self._error is None:
+            m = self._model
+            ints = dict(ints)
+            for sym in m.inputs:
+                ints.setdefault(sym, bound[sym])
+            if not self._batched:
+                ints = {k: v[0] if v.ndim and v.shape[0] == 1 and k not in m._const_syms() else v
+                        for k, v in ints.items()}
+            prog = m.program(self._shards[0][1], "outputs")
+            cycles = {d.label: None for d in prog.devops}
+            self._result = RunOutput(m, ints, cycles, CudaRunResult(self._batch, self._shards, cycles), prog)
+
+    def wait(self) -> RunOutput:
+        with self._model._lock:
+            self._finish()
+            if self in self._model._outstanding:
+                self._model._outstanding.remove(self)
+        if self._error is not None:
+            raise self._error
+        return self._result
+
+
 def _resolve_model(model, example_inputs, calib_inputs, consts, quant_kw, prove=True):
     from .frontend import Quantized
     from .frontend.numerics import prove_no_overflow
@@ -199,6 +261,8 @@ class CompiledModel:
         self._devices = {}           # device -> DeviceModel
         self._pool_size_at_upload = {}
         self._pipes = {}             # device -> [DeviceModel] for pipelined runs
+        self._tail = {}              # device -> the pipelined model that took the latest chunk (cross-call chaining)
+        self._outstanding = []       # PendingRuns of submit() not waited on yet
         self._lock = threading.Lock()
 
     # ------------------------------------------------------------------------------------- programs
@@ -227,6 +291,8 @@ class CompiledModel:
         prog = self.program(size, "outputs")              # lowered first: it may add constants to the pool
         pipes = self._pipes.setdefault(device, {})
         if self._pool_size_at_upload.get(("pipe", device)) != self._pool.size:
+            self._finish_outstanding()                    # no model is freed under queued work
+            self._tail.pop(device, None)
             for ms in pipes.values():
                 for m in ms:
                     m.close()
@@ -237,6 +303,7 @@ class CompiledModel:
             ms.append(DeviceModel(device, self._pool.blob()))
         for m in ms[:count]:
             if m.prepared_key != (size, "outputs"):
+                self._finish_outstanding()
                 m.prepare(prog.ops, prog.plan.arena, key=(size, "outputs"))
         return ms[:count]
 
@@ -379,6 +446,59 @@ class CompiledModel:
             cycles[d.label] = (cycles.get(d.label) or 0) + us if us is not None else None
         return RunOutput(self, ints, cycles, CudaRunResult(batch, shards, cycles), prog, stray)
 
+    def submit(self, x, backend: str = "cuda", *, quantized=False, out=None) -> PendingRun:
+        """run(x, backend, quantized=..., out=...) without waiting: the inputs' copies in, the launch chain and the
+        outputs' copies out are queued on the device(s) behind any earlier submit() or run(), and the returned
+        PendingRun's wait() gives the RunOutput. Consecutive submits overlap one call's copies with another's
+        kernels, which a synchronous run() cannot do across its own start and end. Pass pinned (page-locked) input
+        and `out` arrays: a copy out to pageable memory makes the queuing call itself wait for it. keep="all",
+        timing and guarded runs are synchronous only (use run()); a graph whose outputs are not whole contiguous
+        buffers also runs synchronously here, and its PendingRun is already complete."""
+        if backend not in BACKENDS:
+            raise ValueError(f"unknown backend {backend!r}: this build runs {', '.join(BACKENDS)} (the tiny-gpu "
+                             "simulators isasim/rtl/verilator are not part of it)")
+        bound, batch, batched = self._bind_inputs(x, quantized)
+        out = self._check_out(out, batch)
+        shards = self._shards(batch)
+        with self._lock:
+            plans = {hi - lo: self._chunk_plan(hi - lo, "outputs", False) for _, lo, hi in shards}
+            sync = not all(self._pipelinable(self.program(c, "outputs")) for p in plans.values() for c in set(p))
+        if sync:
+            res = self.run(x, backend, quantized=quantized, out=out)
+            pr = PendingRun(self, batch, batched, [(d, hi - lo) for d, lo, hi in shards], [], (bound, None, {}))
+            pr._tickets, pr._keep, pr._result = None, None, res
+            return pr
+        from .runtime.program import NP
+        full = dict(out)
+        for sym in self.outputs:            # the shards' copies out land straight in these arrays
+            if sym not in full:
+                full[sym] = np.empty((batch,) + tuple(self.meta[sym][1]), dtype=NP[self.meta[sym][2]])
+        with self._lock:
+            self._outstanding = [p for p in self._outstanding if p._tickets is not None]
+            while len(self._outstanding) >= MAX_OUTSTANDING:      # bounded queue: collect the oldest run first
+                self._outstanding.pop(0)._finish()
+            tickets, copies = [], []
+            try:
+                for d, lo, hi in shards:
+                    _, tk, ins = self._enqueue_pipelined(d, {k: v[lo:hi] for k, v in bound.items()}, hi - lo,
+                                                         plans[hi - lo], {k: v[lo:hi] for k, v in full.items()})
+                    tickets += tk
+                    copies.append(ins)
+            except BaseException:
+                _wait_tickets(tickets)
+                raise
+            pr = PendingRun(self, batch, batched, [(d, hi - lo) for d, lo, hi in shards], tickets,
+                            (bound, copies, full))
+            self._outstanding.append(pr)
+        return pr
+
+    def _finish_outstanding(self):
+        """Collect every queued submit() (their errors stay with their PendingRuns); called with the lock held
+        before a device model is re-prepared or freed."""
+        for p in list(self._outstanding):
+            p._finish()
+        self._outstanding = []
+
     def _check_out(self, out, batch):
         if not out:
             return {}
@@ -501,10 +621,22 @@ class CompiledModel:
         return True
 
     def _run_pipelined(self, device, bound, b, plan, out=None):
+        """The shard as a pipelined run (_enqueue_pipelined), waited on before returning."""
+        res, tickets, _ = self._enqueue_pipelined(device, bound, b, plan, out)
+        _wait_tickets(tickets)
+        ints = dict(res)
+        for sym in self.inputs:
+            ints.setdefault(sym, bound[sym])
+        return ints, None
+
+    def _enqueue_pipelined(self, device, bound, b, plan, out=None):
         """The shard as chunks of plan[i] samples, each enqueued on a device model prepared for its size: equal-size
         chunks rotate over PIPELINE_MODELS models (own stream and arena each), so while one chunk's kernels run the
         next chunk's inputs are copied in and the previous chunk's outputs copied out, straight between the
-        caller's arrays and the device."""
+        caller's arrays and the device. The first chunk is chained behind the latest chunk of an earlier call on
+        the device, so back-to-back calls keep the bus and the SMs busy across call boundaries. Returns the output
+        arrays, a completion ticket per model used and the input arrays the copies read (which must outlive the
+        tickets), without waiting."""
         from .runtime.program import NP
         sizes = sorted(set(plan))
         counts = {c: min(PIPELINE_MODELS, plan.count(c)) for c in sizes}
@@ -519,11 +651,15 @@ class CompiledModel:
             else:
                 res[sym] = np.empty(full, dtype=NP[self.meta[sym][2]])
         used = [m for c in sizes for m in models[c]]
+        live = {id(m) for ms in self._pipes.get(device, {}).values() for m in ms}
+        prev = self._tail.get(device)
+        prev = prev if prev is not None and id(prev) in live else None
         for dm in used:
             dm.clear_flags()
         turn = {c: 0 for c in sizes}
+        enqueued = []
         try:
-            lo, prev = 0, None
+            lo = 0
             for c in plan:
                 prog = self.program(c, "outputs")
                 dm = models[c][turn[c] % counts[c]]
@@ -533,20 +669,18 @@ class CompiledModel:
                            [(prog.plan.addresses[v.root], res[sym][lo:hi])
                             for sym, v in self._readable(prog, "outputs").items()],
                            after=prev if prev is not dm else None)
+                if dm not in enqueued:
+                    enqueued.append(dm)
                 lo, prev = hi, dm
-        finally:
-            errs = []
-            for dm in used:
-                try:
-                    dm.wait()
-                except Exception as e:             # every stream drained before the first error is raised
-                    errs.append(e)
-            if errs:
-                raise errs[0]
-        ints = dict(res)
-        for sym in self.inputs:
-            ints.setdefault(sym, bound[sym])
-        return ints, None
+                self._tail[device] = dm
+        except BaseException:
+            # what was queued still runs on the caller's arrays: let it finish before the error propagates
+            try:
+                _wait_tickets([(dm, dm.record()) for dm in enqueued])
+            except Exception:
+                pass
+            raise
+        return res, [(dm, dm.record()) for dm in used], ins
 
     def _readable(self, prog, keep):
         want = {}

@@ -30,7 +30,7 @@ KIND_NAMES = {OP_GEMM: "gemm", OP_LUT: "lut", OP_LUT_MUL: "lut_mul", OP_ADD_REQU
 
 EXPORTS = ("anvil_abi_version", "anvil_last_error", "anvil_device_count", "anvil_cuda_init", "anvil_model_create",
            "anvil_model_prepare", "anvil_model_run", "anvil_model_enqueue", "anvil_model_clear_flags",
-           "anvil_model_wait", "anvil_model_selftest_timeout", "anvil_model_run_device", "anvil_model_read",
+           "anvil_model_wait", "anvil_model_record", "anvil_model_wait_ticket", "anvil_model_selftest_timeout", "anvil_model_run_device", "anvil_model_read",
            "anvil_model_write", "anvil_model_read_const", "anvil_model_arena", "anvil_model_describe",
            "anvil_model_free",
            "anvil_gemm_requant")
@@ -77,6 +77,8 @@ def load_library(path: str | os.PathLike | None = None):
             "anvil_model_enqueue": ([vp, ctypes.POINTER(AnvilIO), i32, ctypes.POINTER(AnvilIO), i32, vp], i32),
             "anvil_model_clear_flags": ([vp], i32),
             "anvil_model_wait": ([vp], i32),
+            "anvil_model_record": ([vp, ctypes.POINTER(u64)], i32),
+            "anvil_model_wait_ticket": ([vp, u64], i32),
             "anvil_model_selftest_timeout": ([vp, u64], i32),
             "anvil_model_read": ([vp, u64, vp, u64], i32),
             "anvil_model_write": ([vp, u64, vp, u64], i32),
@@ -156,6 +158,17 @@ class DeviceModel:
     def wait(self):
         """Synchronise this model's stream and raise if a device check fired since clear_flags()."""
         check(self.lib.anvil_model_wait(self._h), "anvil_model_wait")
+
+    def record(self) -> int:
+        """anvil_model_record: a ticket for everything enqueued on this model so far (its device checks are
+        snapshotted and cleared in stream order)."""
+        t = ctypes.c_uint64(0)
+        check(self.lib.anvil_model_record(self._h, ctypes.byref(t)), "anvil_model_record")
+        return t.value
+
+    def wait_ticket(self, ticket: int):
+        """Block until the ticket's work is done; raise if a device check fired in it."""
+        check(self.lib.anvil_model_wait_ticket(self._h, int(ticket)), "anvil_model_wait_ticket")
 
     def selftest_timeout(self, wait_ns: int):
         """Run the device wait-bound self-test: raises TimeoutError after about wait_ns (the expected outcome)."""

@@ -136,6 +136,14 @@ struct anvil_model {
   // pipelined enqueues: recorded after this model's last input copies and after its last launch chain
   cudaEvent_t ev_in = nullptr, ev_run = nullptr;
   int pair_clusters = -1;            // co-resident CTA pairs of the pair GEMM (0: the pair path is off)
+  // completion tickets (anvil_model_record / anvil_model_wait_ticket): ticket t owns ring slot t % TICKETS, which
+  // holds the event recorded after the work it covers and a device snapshot of the check words at that point
+  static constexpr int TICKETS = 64;
+  uint32_t *ticket_flags = nullptr;  // TICKETS x FLAG_WORDS device words
+  cudaEvent_t ticket_ev[TICKETS] = {};
+  bool ticket_pending[TICKETS] = {};
+  uint64_t ticket_next = 0;
+  cudaStream_t status_stream = nullptr;   // reads the snapshots without queueing behind the model's stream
 };
 
 extern "C" int anvil_device_count(int *count) {
@@ -282,6 +290,10 @@ extern "C" void anvil_model_free(anvil_model *m) {
   for (auto e : m->events) cudaEventDestroy(e);
   if (m->ev_in) cudaEventDestroy(m->ev_in);
   if (m->ev_run) cudaEventDestroy(m->ev_run);
+  for (auto e : m->ticket_ev)
+    if (e) cudaEventDestroy(e);
+  if (m->ticket_flags) cudaFree(m->ticket_flags);
+  if (m->status_stream) cudaStreamDestroy(m->status_stream);
   if (m->arena) cudaFree(m->arena);
   if (m->consts) cudaFree(m->consts);
   if (m->flags) cudaFree(m->flags);
@@ -1071,6 +1083,46 @@ extern "C" int anvil_model_wait(anvil_model *m) {
   uint32_t hflags[FLAG_WORDS];
   CK(cudaMemcpyAsync(hflags, m->flags, sizeof hflags, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
+  return check_flags(m, hflags);
+}
+
+// Completion tickets: the asynchronous form of anvil_model_wait. A ticket marks everything enqueued on the model's
+// stream so far; the check words that work raised are snapshotted into the ticket's slot and then cleared in stream
+// order, so each ticket reports exactly the checks of the work between the previous ticket (or clear_flags) and
+// itself, however much later work has been enqueued behind it by the time it is waited on.
+extern "C" int anvil_model_record(anvil_model *m, uint64_t *ticket) {
+  if (!m || !ticket) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_record");
+  CK(cudaSetDevice(m->device));
+  const int slot = (int)(m->ticket_next % anvil_model::TICKETS);
+  if (m->ticket_pending[slot])
+    return fail(ANVIL_E_BAD_ARG, "anvil_model_record: %d tickets are outstanding on this model; wait on the oldest "
+                "first", anvil_model::TICKETS);
+  if (!m->ticket_flags) CK(cudaMalloc(&m->ticket_flags, anvil_model::TICKETS * FLAG_WORDS * sizeof(uint32_t)));
+  if (!m->status_stream) CK(cudaStreamCreateWithFlags(&m->status_stream, cudaStreamNonBlocking));
+  if (!m->ticket_ev[slot]) CK(cudaEventCreateWithFlags(&m->ticket_ev[slot], cudaEventDisableTiming));
+  uint32_t *snap = m->ticket_flags + slot * FLAG_WORDS;
+  CK(cudaMemcpyAsync(snap, m->flags, FLAG_WORDS * sizeof(uint32_t), cudaMemcpyDeviceToDevice, m->stream));
+  CK(cudaMemsetAsync(m->flags, 0, FLAG_WORDS * sizeof(uint32_t), m->stream));
+  CK(cudaEventRecord(m->ticket_ev[slot], m->stream));
+  m->ticket_pending[slot] = true;
+  *ticket = m->ticket_next++;
+  return ANVIL_OK;
+}
+
+extern "C" int anvil_model_wait_ticket(anvil_model *m, uint64_t ticket) {
+  if (!m) return fail(ANVIL_E_BAD_ARG, "model is NULL");
+  const int slot = (int)(ticket % anvil_model::TICKETS);
+  if (ticket >= m->ticket_next || m->ticket_next - ticket > (uint64_t)anvil_model::TICKETS ||
+      !m->ticket_pending[slot])
+    return fail(ANVIL_E_BAD_ARG, "anvil_model_wait_ticket: ticket %llu is not outstanding on this model",
+                (unsigned long long)ticket);
+  CK(cudaSetDevice(m->device));
+  CK(cudaEventSynchronize(m->ticket_ev[slot]));
+  uint32_t hflags[FLAG_WORDS];
+  CK(cudaMemcpyAsync(hflags, m->ticket_flags + slot * FLAG_WORDS, sizeof hflags, cudaMemcpyDeviceToHost,
+                     m->status_stream));
+  CK(cudaStreamSynchronize(m->status_stream));
+  m->ticket_pending[slot] = false;
   return check_flags(m, hflags);
 }
 

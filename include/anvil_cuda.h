@@ -166,6 +166,17 @@ ANVIL_API int anvil_model_enqueue(anvil_model *m, const anvil_io *inputs, int n_
 ANVIL_API int anvil_model_clear_flags(anvil_model *m);
 ANVIL_API int anvil_model_wait(anvil_model *m);
 
+/* Completion tickets, the asynchronous form of anvil_model_wait: anvil_model_record marks everything enqueued on
+ * the model's stream so far (it snapshots the device check words on the device and clears them, both in stream
+ * order, then records an event) and returns a ticket; anvil_model_wait_ticket blocks until that work is done and
+ * maps the checks it raised to a status as anvil_model_wait does, unaffected by work enqueued after the ticket, so a
+ * caller can keep the next calls' copies and kernels queued while it waits on an earlier one. At most 64 tickets
+ * per model are outstanding (a 65th record fails with ANVIL_E_BAD_ARG); each is waited on once. Backs
+ * CompiledModel.submit / PendingRun.wait (asynchronous runs of the reference's CompiledModel.run,
+ * anvil/driver.py:305-322); the reference has no asynchronous entry point of its own. */
+ANVIL_API int anvil_model_record(anvil_model *m, uint64_t *ticket);
+ANVIL_API int anvil_model_wait_ticket(anvil_model *m, uint64_t ticket);
+
 /* Self-test of the device-side wait bound every kernel relies on: launches one block whose warps wait, through
  * the same bounded mbarrier wait, on a barrier nothing arrives on, with a limit of `wait_ns` (at most the kernels'
  * own 2 s). The wait gives up and raises the timeout flag, so the call returns ANVIL_E_TIMEOUT after about wait_ns,

@@ -222,6 +222,50 @@ def test_auto_pipeline_matches_the_oracle(monkeypatch):
     _check(cm.run(xs, "cuda", quantized=True).ints, want.values, cm.outputs)
 
 
+def test_submitted_runs_match_the_oracle():
+    """Runs queued with submit() (each chained behind the previous call's chunks, waited on out of order, outputs
+    into pinned caller buffers) give the oracle's outputs, the same as run()."""
+    import torch
+    module, consts, body = _frozen()
+    rng = np.random.default_rng(23)
+    cm = anvil.compile(module, consts=consts, params=CudaParams(pipeline=4))
+    o = cm.outputs[0]
+    xs = [rng.integers(-(1 << 15), 1 << 15, (8,) + np.shape(body["x"])) for _ in range(5)]
+    bufs = [torch.zeros((8,) + tuple(cm.meta[o][1]), dtype=torch.int16, pin_memory=True).numpy() for _ in xs]
+    pend = [cm.submit(x, "cuda", quantized=True, out={o: b}) for x, b in zip(xs, bufs)]
+    for i in (3, 0, 4, 1, 2):
+        res = pend[i].wait()
+        want = interp.run(module, {"x": xs[i]}, consts, batch=True)
+        assert res.ints[o] is bufs[i]
+        _check(res.ints, want.values, cm.outputs)
+    _check(cm.run(xs[0], "cuda", quantized=True).ints, interp.run(module, {"x": xs[0]}, consts, batch=True).values,
+           cm.outputs)
+
+
+def test_submitted_overflow_belongs_to_its_run():
+    """A checked overflow in one queued run raises from that run's wait() only; the runs queued before and after
+    it return their outputs."""
+    from anvil.ir import GraphBuilder
+    g = GraphBuilder("ovf")
+    x = g.input("x", [4, 32])
+    w = g.const("w", [32, 8])
+    g.output(g.qlinear("y", x, w, 1 << 20, 4))
+    m = g.module()
+    c = {"w": np.full((32, 8), 127)}
+    cm = anvil.compile(m, consts=c, prove=False, params=CudaParams(pipeline=3))
+    zeros = np.zeros((6, 4, 32), dtype=np.int64)
+    bad = zeros.copy()
+    bad[4] = 127                                     # only the third chunk of this run overflows
+    small = np.zeros((6, 4, 32), dtype=np.int64)
+    small[:, :, :8] = np.random.default_rng(24).integers(0, 2, (6, 4, 8))     # acc <= 8 * 127: acc*M fits int32
+    p1, p2, p3 = cm.submit(zeros, quantized=True), cm.submit(bad, quantized=True), cm.submit(small, quantized=True)
+    want = interp.run(m, {"x": small}, c, batch=True)
+    _check(p3.wait().ints, want.values, cm.outputs)
+    with pytest.raises(OverflowError):
+        p2.wait()
+    assert not p1.wait().ints["y"].any()
+
+
 def test_device_replays_keep_the_inputs():
     """anvil_model_run_device replays the chain on the arena (the bench's device-timed loop): the graph inputs are
     never reused by the memory plan, so after several replays the outputs still equal the oracle's (config c2,
