@@ -360,24 +360,34 @@ __global__ void __launch_bounds__(256, NV8 == 1 ? 5 : NV8 == 2 ? 4 : NV8 == 3 ? 
     }
   };
 
-  // two row buffers in turn: the next row's vectors are in flight while the current row is computed
-  uint2 xa[NV8], xb[NV8];
+  // three row buffers in turn: the next two rows' vectors are in flight while the current row is computed
+  uint2 xa[NV8], xb[NV8], xc[NV8];
 #pragma unroll
   for (int v = 0; v < NV8; ++v) xa[v] = xp[32 * v];
-  for (int i = 0; i < nr; i += 2) {
-    if (i + 1 < nr) {
+  if (nr > 1) {
 #pragma unroll
-      for (int v = 0; v < NV8; ++v) xb[v] = xp[step + 32 * v];
+    for (int v = 0; v < NV8; ++v) xb[v] = xp[step + 32 * v];
+  }
+  for (int i = 0; i < nr; i += 3) {
+    if (i + 2 < nr) {
+#pragma unroll
+      for (int v = 0; v < NV8; ++v) xc[v] = xp[2 * step + 32 * v];
     }
     row_out(xa, op);
     if (i + 1 >= nr) break;
-    if (i + 2 < nr) {
+    if (i + 3 < nr) {
 #pragma unroll
-      for (int v = 0; v < NV8; ++v) xa[v] = xp[2 * step + 32 * v];
+      for (int v = 0; v < NV8; ++v) xa[v] = xp[3 * step + 32 * v];
     }
     row_out(xb, op + step);
-    xp += 2 * step;
-    op += 2 * step;
+    if (i + 2 >= nr) break;
+    if (i + 4 < nr) {
+#pragma unroll
+      for (int v = 0; v < NV8; ++v) xb[v] = xp[4 * step + 32 * v];
+    }
+    row_out(xc, op + 2 * step);
+    xp += 3 * step;
+    op += 3 * step;
   }
 }
 

@@ -90,6 +90,7 @@ class ClockSampler:
 
     def __init__(self, device):
         self.device, self.sm, self.max, self.reasons, self._stop = device, [], None, set(), False
+        self.times, self.err = [], None
 
     def __enter__(self):
         try:
@@ -99,9 +100,10 @@ class ClockSampler:
             idx = int(vis.split(",")[self.device]) if vis else self.device
             self.h, self.nv = nv.nvmlDeviceGetHandleByIndex(idx), nv
             self.max = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
-        except Exception:
-            self.nv = None
+        except Exception as e:
+            self.nv, self.err = None, f"{type(e).__name__}: {e}"[:120]
         self.t = threading.Thread(target=self._run, daemon=True)
+        self.t0 = time.perf_counter()
         self.t.start()
         return self
 
@@ -110,13 +112,15 @@ class ClockSampler:
             if self.nv is not None:
                 try:
                     self.sm.append(float(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)))
+                    self.times.append(time.perf_counter() - self.t0)
                     r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
                     self.reasons |= {k for k, bit in self.REASONS.items() if r & bit}
-                except Exception:
-                    self.nv = None
-            time.sleep(0.005)
+                except Exception as e:
+                    self.nv, self.err = None, f"{type(e).__name__}: {e}"[:120]
+            time.sleep(0.002)
 
     def __exit__(self, *a):
+        self.region_s = time.perf_counter() - self.t0
         self._stop = True
         self.t.join(timeout=2)
         if not self.sm:                          # NVML unavailable: one nvidia-smi reading
@@ -129,8 +133,13 @@ class ClockSampler:
                 pass
 
     def summary(self):
-        return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.max,
-                "reasons": sorted(self.reasons), "samples": len(self.sm)}
+        out = {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.max,
+               "reasons": sorted(self.reasons), "samples": len(self.sm),
+               "region_ms": round(1000 * getattr(self, "region_s", 0.0), 2),
+               "sample_ms": [round(1000 * t, 2) for t in (self.times[:1] + self.times[-1:])]}
+        if self.err:
+            out["nvml_error"] = self.err
+        return out
 
 
 def _dist():

@@ -98,7 +98,8 @@ def test_queued_runs_match_the_oracle_in_any_wait_order(emu_models):
     assert cm._outstanding == []
 
 
-def test_chunks_chain_across_calls(emu_models):
+def test_chunks_chain_across_calls(emu_models, monkeypatch):
+    monkeypatch.setattr(D, "PIPELINE_MODELS", 4)
     cm = _compiled()
     p1 = cm.submit(_inputs(8, 1), quantized=True)
     models = list(EmuModel.instances)
