@@ -217,3 +217,22 @@ def test_two_devices_in_one_process():
     assert [d for d, _ in res.result.shards] == [0, 1] and [b for _, b in res.result.shards] == [3, 2]
     for s in cm.outputs:
         _equal(res.ints[s], want.values[s], s)
+
+
+def test_two_devices_submitted():
+    """submit() with CudaParams(devices=(0, 1)): each device's shard is queued on that device's models without a
+    host thread per device; two runs queued back to back, waited in reverse order, equal the oracle (needs two
+    GPUs)."""
+    torch = _torch()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from anvil import workloads as W
+    cm, gen = W.compile_config("c3", params=CudaParams(devices=(0, 1)))
+    xs = [cm.quantize_input(gen(4)), cm.quantize_input(gen(4))[::-1].copy()]
+    pend = [cm.submit(x, "cuda", quantized=True) for x in xs]
+    for x, p in reversed(list(zip(xs, pend))):
+        res = p.wait()
+        assert [d for d, _ in res.result.shards] == [0, 1]
+        want = interp.run(cm.module, {cm.inputs[0]: x}, cm.consts, batch=True)
+        for s in cm.outputs:
+            _equal(res.ints[s], want.values[s], s)
