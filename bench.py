@@ -378,13 +378,18 @@ def run_ours(args):
             o[s_] = torch.empty(shape, dtype={"i8": torch.int8, "i16": torch.int16, "i32": torch.int32}[dt],
                                 pin_memory=True).numpy()
         return o
-    outs = [pinned_outs() for _ in range(2)]     # a buffer is reused only after the step that filled it was waited on
+    out_step = sum(int(np.prod(cm.meta[s_][1])) * batch * {"i8": 1, "i16": 2, "i32": 4}[cm.meta[s_][2]]
+                   for s_ in cm.outputs)
+    # two steps in flight need two output buffers (a buffer is reused only after the step that filled it was waited
+    # on); above 8 GB of output per step (c5's logits) one pinned buffer and one step in flight
+    depth = 2 if out_step <= (8 << 30) else 1
+    outs = [pinned_outs() for _ in range(depth)]
 
     def submitted(n):
         pend, last = [], None
         for step in range(n):
-            pend.append(cm.submit(xin, "cuda", quantized=True, out=outs[step % 2]))
-            if len(pend) > 1:
+            pend.append(cm.submit(xin, "cuda", quantized=True, out=outs[step % depth]))
+            if len(pend) >= depth:
                 last = pend.pop(0).wait()
         for p_ in pend:
             last = p_.wait()
@@ -416,7 +421,7 @@ def run_ours(args):
                        "launches": len(prog.ops), "fusions": prog.fused},
             "e2e": {"value": ws * tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(xin.nbytes),
                     "d2h_bytes_per_step": int(out_bytes), "api": "cm.submit(x, 'cuda', quantized=True, out=...) "
-                    "then .wait() on the previous step (two steps in flight)",
+                    "then .wait() on the previous step", "steps_in_flight": depth,
                     "run_value": ws * tokens / run_s, "run_api": "cm.run(x, 'cuda', quantized=True, out=...) per "
                     "step (synchronous)",
                     "bus_ms_per_step": bus_ms,
