@@ -28,10 +28,10 @@ import numpy as np
 from .ir import graph as g
 
 BACKENDS = ("cuda",)
-PIPELINE_MODELS = 3          # device models (arenas + streams) a pipelined run rotates over
+PIPELINE_MODELS = 4          # device models (arenas + streams) a pipelined run rotates over
 PIPELINE_TOKENS = 8192       # "auto" pipeline chunk size, in tokens. c3 batch 64 on one B200, pinned buffers, calls
-                             # queued by submit(): 8 chunks over 3 models 1.30-1.45 ms per call, over 4 models
-                             # 1.38-1.44 ms, 5-8 models slower; 4 chunks 1.51 ms, 16 chunks 1.71-1.75 ms
+                             # queued by submit(), copies on the device's shared copy streams: 8 chunks over 4 models
+                             # 1.23 ms per call, over 3 models 1.30 ms; 4 chunks 1.30 ms, 16 chunks 1.67 ms
 NOMINAL_PEAKS = {"int8_tops": 4500.0, "hbm_gbs": 7700.0}    # B200 dense int8 tensor and HBM3e, NVIDIA's figures
 GUARD_BYTES = 256            # canary bytes after every buffer of a guarded (stray-write checked) run
 MAX_OUTSTANDING = 32         # submit() calls queued at once (each holds one completion ticket per device model)

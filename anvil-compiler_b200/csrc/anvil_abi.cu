@@ -144,7 +144,42 @@ struct anvil_model {
   bool ticket_pending[TICKETS] = {};
   uint64_t ticket_next = 0;
   cudaStream_t status_stream = nullptr;   // reads the snapshots without queueing behind the model's stream
+  cudaEvent_t ticket_snap[TICKETS] = {};  // after the snapshot, on the model's stream
+  // pipelined enqueues move their copies to the device's shared copy streams: recorded after this model's last
+  // copies out (the arena is free again once it completes)
+  cudaEvent_t ev_free = nullptr;
+  bool free_pending = false;
 };
+
+// The device's two copy streams for pipelined enqueues (one for copies in, one for copies out), shared by every
+// model on the device and kept until the process exits: chunks queued from several models reach the bus back to
+// back in enqueue order, with no cross-stream wait between consecutive copies of one direction.
+struct CopyStreams {
+  std::once_flag once;
+  cudaStream_t in = nullptr, out = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+static CopyStreams g_copy_streams[64];
+
+static int copy_streams(int dev, cudaStream_t *in, cudaStream_t *out) {
+  if (dev < 0 || dev >= 64) return fail(ANVIL_E_BAD_ARG, "device %d out of range", dev);
+  CopyStreams &c = g_copy_streams[dev];
+  std::call_once(c.once, [&]() {
+    c.err = cudaStreamCreateWithFlags(&c.in, cudaStreamNonBlocking);
+    if (c.err == cudaSuccess) c.err = cudaStreamCreateWithFlags(&c.out, cudaStreamNonBlocking);
+  });
+  if (c.err != cudaSuccess) return fail(ANVIL_E_CUDA, "copy stream creation failed: %s", cudaGetErrorString(c.err));
+  *in = c.in;
+  *out = c.out;
+  return ANVIL_OK;
+}
+
+// Orders the model's own stream after its last pipelined copies out (which run on the device's copy-out stream):
+// every path that touches the arena from the model's stream goes through here first.
+static int join_copies(anvil_model *m) {
+  if (m->free_pending) CK(cudaStreamWaitEvent(m->stream, m->ev_free, 0));
+  return ANVIL_OK;
+}
 
 extern "C" int anvil_device_count(int *count) {
   int n = 0;
@@ -285,6 +320,10 @@ static int set_kernel_attrs() {
 extern "C" void anvil_model_free(anvil_model *m) {
   if (!m) return;
   cudaSetDevice(m->device);
+  if (m->free_pending) cudaEventSynchronize(m->ev_free);
+  for (auto e : m->ticket_snap)
+    if (e) cudaEventDestroy(e);
+  if (m->ev_free) cudaEventDestroy(m->ev_free);
   if (m->stream) cudaStreamSynchronize(m->stream);
   if (m->graph) cudaGraphExecDestroy(m->graph);
   for (auto e : m->events) cudaEventDestroy(e);
@@ -716,6 +755,7 @@ static int prepare_op(anvil_model *m, Launch &L) {
 extern "C" int anvil_model_prepare(anvil_model *m, const anvil_op *ops, int n_ops, uint64_t arena_bytes) {
   if (!m || (n_ops && !ops) || n_ops < 0) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_prepare");
   CK(cudaSetDevice(m->device));
+  if (m->free_pending) CK(cudaEventSynchronize(m->ev_free));
   CK(cudaStreamSynchronize(m->stream));
   if (m->graph) {
     cudaGraphExecDestroy(m->graph);
@@ -977,6 +1017,7 @@ extern "C" int anvil_model_run(anvil_model *m, const anvil_io *inputs, int n_inp
   if (!m) return fail(ANVIL_E_BAD_ARG, "model is NULL");
   CK(cudaSetDevice(m->device));
   cudaStream_t st = m->stream;
+  if (int rc = join_copies(m)) return rc;
   for (int i = 0; i < n_inputs; ++i) {
     const anvil_io &io = inputs[i];
     if (io.offset > m->arena_bytes || io.bytes > m->arena_bytes - io.offset)
@@ -1054,19 +1095,31 @@ extern "C" int anvil_model_enqueue(anvil_model *m, const anvil_io *inputs, int n
   if ((rc = ensure_graph(m))) return rc;
   if (!m->ev_in) CK(cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming));
   if (!m->ev_run) CK(cudaEventCreateWithFlags(&m->ev_run, cudaEventDisableTiming));
-  // chained behind `after`: the copies in start once its copies in are done (one chunk at a time at full bus
-  // speed), the launch chain once its chain is done (one chunk's kernels on the SMs at a time)
-  if (after && after->ev_in) CK(cudaStreamWaitEvent(st, after->ev_in, 0));
+  if (!m->ev_free) CK(cudaEventCreateWithFlags(&m->ev_free, cudaEventDisableTiming));
+  cudaStream_t sin, sout;
+  if ((rc = copy_streams(m->device, &sin, &sout))) return rc;
+  // copies in on the device's copy-in stream, once this arena's previous chunk has been copied out (and after
+  // whatever ran on the model's own stream); copies of consecutive chunks follow each other in that one stream
+  if (m->free_pending) CK(cudaStreamWaitEvent(sin, m->ev_free, 0));
+  CK(cudaEventRecord(m->ev_in, st));
+  CK(cudaStreamWaitEvent(sin, m->ev_in, 0));
   for (int i = 0; i < n_inputs; ++i)
     CK(cudaMemcpyAsync(static_cast<uint8_t *>(m->arena) + inputs[i].offset, inputs[i].host, inputs[i].bytes,
-                       cudaMemcpyHostToDevice, st));
-  CK(cudaEventRecord(m->ev_in, st));
+                       cudaMemcpyHostToDevice, sin));
+  CK(cudaEventRecord(m->ev_in, sin));
+  // the launch chain on the model's stream once its inputs are in and `after`'s chain is done (one chunk's
+  // kernels on the SMs at a time)
+  CK(cudaStreamWaitEvent(st, m->ev_in, 0));
   if (after && after->ev_run) CK(cudaStreamWaitEvent(st, after->ev_run, 0));
   CK(cudaGraphLaunch(m->graph, st));
   CK(cudaEventRecord(m->ev_run, st));
+  // copies out on the device's copy-out stream once the chain is done
+  CK(cudaStreamWaitEvent(sout, m->ev_run, 0));
   for (int i = 0; i < n_outputs; ++i)
     CK(cudaMemcpyAsync(outputs[i].host, static_cast<uint8_t *>(m->arena) + outputs[i].offset, outputs[i].bytes,
-                       cudaMemcpyDeviceToHost, st));
+                       cudaMemcpyDeviceToHost, sout));
+  CK(cudaEventRecord(m->ev_free, sout));
+  m->free_pending = true;
   return ANVIL_OK;
 }
 
@@ -1083,6 +1136,7 @@ extern "C" int anvil_model_wait(anvil_model *m) {
   uint32_t hflags[FLAG_WORDS];
   CK(cudaMemcpyAsync(hflags, m->flags, sizeof hflags, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
+  if (m->free_pending) CK(cudaEventSynchronize(m->ev_free));
   return check_flags(m, hflags);
 }
 
@@ -1103,7 +1157,17 @@ extern "C" int anvil_model_record(anvil_model *m, uint64_t *ticket) {
   uint32_t *snap = m->ticket_flags + slot * FLAG_WORDS;
   CK(cudaMemcpyAsync(snap, m->flags, FLAG_WORDS * sizeof(uint32_t), cudaMemcpyDeviceToDevice, m->stream));
   CK(cudaMemsetAsync(m->flags, 0, FLAG_WORDS * sizeof(uint32_t), m->stream));
-  CK(cudaEventRecord(m->ticket_ev[slot], m->stream));
+  if (m->free_pending) {
+    // the ticket also covers this model's copies out, queued on the device's copy-out stream
+    cudaStream_t sin, sout;
+    if (int rc = copy_streams(m->device, &sin, &sout)) return rc;
+    if (!m->ticket_snap[slot]) CK(cudaEventCreateWithFlags(&m->ticket_snap[slot], cudaEventDisableTiming));
+    CK(cudaEventRecord(m->ticket_snap[slot], m->stream));
+    CK(cudaStreamWaitEvent(sout, m->ticket_snap[slot], 0));
+    CK(cudaEventRecord(m->ticket_ev[slot], sout));
+  } else {
+    CK(cudaEventRecord(m->ticket_ev[slot], m->stream));
+  }
   m->ticket_pending[slot] = true;
   *ticket = m->ticket_next++;
   return ANVIL_OK;
@@ -1130,6 +1194,7 @@ extern "C" int anvil_model_run_device(anvil_model *m, int iters, int use_graph, 
   if (!m || iters < 1) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_run_device");
   CK(cudaSetDevice(m->device));
   cudaStream_t st = m->stream;
+  if (int rc = join_copies(m)) return rc;
   if (use_graph) {
     int rc = ensure_graph(m);
     if (rc) return rc;
@@ -1165,6 +1230,7 @@ extern "C" int anvil_model_read(anvil_model *m, uint64_t offset, void *host, uin
   if (!m || !host) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_read");
   if (offset > m->arena_bytes || bytes > m->arena_bytes - offset) return fail(ANVIL_E_BAD_ARG, "read outside the arena");
   CK(cudaSetDevice(m->device));
+  if (int rc = join_copies(m)) return rc;
   CK(cudaMemcpyAsync(host, static_cast<uint8_t *>(m->arena) + offset, bytes, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
   return ANVIL_OK;
@@ -1174,6 +1240,7 @@ extern "C" int anvil_model_write(anvil_model *m, uint64_t offset, const void *ho
   if (!m || !host) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_write");
   if (offset > m->arena_bytes || bytes > m->arena_bytes - offset) return fail(ANVIL_E_BAD_ARG, "write outside the arena");
   CK(cudaSetDevice(m->device));
+  if (int rc = join_copies(m)) return rc;
   CK(cudaMemcpyAsync(static_cast<uint8_t *>(m->arena) + offset, host, bytes, cudaMemcpyHostToDevice, m->stream));
   CK(cudaStreamSynchronize(m->stream));
   return ANVIL_OK;

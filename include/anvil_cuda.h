@@ -152,15 +152,19 @@ ANVIL_API int anvil_model_run_device(anvil_model *m, int iters, int use_graph, f
 
 /* The run of anvil_model_run split for pipelines over several models (each its own arena and stream): the H2D
  * copies of `inputs`, the launch chain (one CUDA graph launch, captured on first use) and the D2H copies of
- * `outputs`, all enqueued on the model's stream, returning without waiting. With `after` (another model on the
- * same device, or NULL) the copies in wait for `after`'s latest copies in and the launch chain for `after`'s
- * latest launch chain, so a batch enqueued chunk by chunk round-robin over two or more models, each chunk after
- * the previous one's model, runs as a copy-in / compute / copy-out pipeline: one chunk's kernels at a time, with
- * the next chunk's input and the previous chunk's output crossing the bus meanwhile (the host buffers should be
- * pinned, and must stay valid until anvil_model_wait returns). Device flags persist across enqueues:
- * anvil_model_clear_flags resets them (stream-ordered) and anvil_model_wait synchronises the stream and maps any
- * raised flag to its status, as anvil_model_run does. The pipelined form of the reference's CompiledModel.run
- * (anvil/driver.py:305-322); no separate reference entry point. */
+ * `outputs`, returning without waiting. The copies go to the device's two shared copy streams (one per direction,
+ * created on first use and kept until exit), in enqueue order, so the copies of consecutive enqueues, from
+ * whichever models, follow each other on the bus with no wait in between; a model's copies in start once its
+ * previous enqueue's copies out are done, its launch chain (on the model's stream) once its copies in are done,
+ * and with `after` (another model on the same device, or NULL) once `after`'s latest launch chain is done too. A
+ * batch enqueued chunk by chunk round-robin over two or more models, each chunk after the previous one's model,
+ * runs as a copy-in / compute / copy-out pipeline: one chunk's kernels at a time, with the next chunk's input and
+ * the previous chunk's output crossing the bus meanwhile (the host buffers should be pinned, and must stay valid
+ * until anvil_model_wait returns). Every other call that touches the arena first waits for the model's pending
+ * copies out. Device flags persist across enqueues: anvil_model_clear_flags resets them (stream-ordered) and
+ * anvil_model_wait synchronises the model (its stream and its copies out) and maps any raised flag to its status,
+ * as anvil_model_run does. The pipelined form of the reference's CompiledModel.run (anvil/driver.py:305-322); no
+ * separate reference entry point. */
 ANVIL_API int anvil_model_enqueue(anvil_model *m, const anvil_io *inputs, int n_inputs, const anvil_io *outputs,
                                   int n_outputs, anvil_model *after);
 ANVIL_API int anvil_model_clear_flags(anvil_model *m);
