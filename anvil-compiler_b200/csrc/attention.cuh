@@ -432,8 +432,13 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
 #pragma unroll
           for (int q = 0; q < 32; ++q) mx = max(mx, v[q]);
         } else {
+          // masked columns are stored as -128: a value no kept score exceeds the row max with, so every LUT index
+          // below stays in [0, 255] without a clamp
 #pragma unroll
-          for (int q = 0; q < 32; ++q) mx = max(mx, cb + q < kept ? v[q] : -128);
+          for (int q = 0; q < 32; ++q) {
+            v[q] = cb + q < kept ? v[q] : -128;
+            mx = max(mx, v[q]);
+          }
         }
         uint32_t wq[8];
 #pragma unroll
@@ -468,7 +473,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
       if (stop) { stopped = true; break; }
       mx = max(max(red_max[r], red_max[128 + r]), max(red_max[256 + r], red_max[384 + r]));
       // a kept score x <= mx (a signed byte of the slab) has lut[x - mx + 255] at lut_at(lutc, x) in this lane's
-      // copy; a masked column's byte may exceed mx and is clamped to it first, so every index is in [0, 255]
+      // copy; a masked column holds -128 (stored so by the drain), so every index is in [0, 255]
       const uint32_t lutc = smem_u32(lut + (255 - mx) * Cfg::LUT_COPIES + lcopy);
       // pass A: partial S = sum over this part's kept columns of lut[x - max + 255]
       int tot0 = 0, tot1 = 0;
@@ -487,11 +492,15 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
             tot1 += lut_byte<Cfg::LUT_COPIES, 2>(lutc, wv[q]) + lut_byte<Cfg::LUT_COPIES, 3>(lutc, wv[q]);
           }
         } else {
+          // all 32 looked up as in the full case; the masked ones (stored as -128) are taken out again as a count
+          // times lut[-128 - max + 255]
 #pragma unroll
-          for (int q = 0; q < 32; ++q) {
-            const int e = lut_at<Cfg::LUT_COPIES>(lutc, min(sbyte_prmt(wv[q >> 2], q & 3), mx));
-            tot0 += cb + q < kept ? e : 0;
+          for (int q = 0; q < 8; ++q) {
+            tot0 += lut_byte<Cfg::LUT_COPIES, 0>(lutc, wv[q]) + lut_byte<Cfg::LUT_COPIES, 1>(lutc, wv[q]);
+            tot1 += lut_byte<Cfg::LUT_COPIES, 2>(lutc, wv[q]) + lut_byte<Cfg::LUT_COPIES, 3>(lutc, wv[q]);
           }
+          const int nmask = 32 - min(32, max(0, kept - cb));
+          tot0 -= nmask * lut_at<Cfg::LUT_COPIES>(lutc, -128);
         }
       }
       red_sum[part * 128 + r] = tot0 + tot1;
@@ -527,8 +536,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
           } else {
 #pragma unroll
             for (int q = 0; q < 32; ++q) {
-              const int x = min(sbyte_prmt(wv[q >> 2], q & 3), mx);
-              const unsigned num = (unsigned)lut_at<Cfg::LUT_COPIES>(lutc, x) * one2 + half2;
+              const unsigned num = (unsigned)lut_byte_q<Cfg::LUT_COPIES>(lutc, wv[q >> 2], q & 3) * one2 + half2;
               pv[q] = cb + q < kept ? (int)(__umulhi(num, magic) >> msh) : 0;
             }
           }
