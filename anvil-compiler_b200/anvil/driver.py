@@ -171,6 +171,8 @@ class PendingRun:
             self._result = RunOutput(m, ints, cycles, CudaRunResult(self._batch, self._shards, cycles), prog)
 
     def wait(self) -> RunOutput:
+        """Block until the run is done (holding the model's lock, so a submit() from another thread waits for it);
+        return its RunOutput or raise its device error, again on every later call."""
         with self._model._lock:
             self._finish()
             if self in self._model._outstanding:

@@ -266,6 +266,25 @@ def test_submitted_overflow_belongs_to_its_run():
     assert not p1.wait().ints["y"].any()
 
 
+def test_completion_tickets_are_bounded_and_single_use():
+    """anvil_model_record keeps at most 64 outstanding tickets per model (the 65th is refused with ValueError and
+    nothing is queued for it); each ticket is waited on once, in any order, and a ticket already waited on (or never
+    issued) is refused."""
+    module, consts, _ = _frozen()
+    cm = anvil.compile(module, consts=consts)
+    dm = cm._device_model(0)
+    tickets = [dm.record() for _ in range(64)]
+    with pytest.raises(ValueError, match="outstanding"):
+        dm.record()
+    for t in reversed(tickets):
+        dm.wait_ticket(t)
+    with pytest.raises(ValueError, match="not outstanding"):
+        dm.wait_ticket(tickets[0])
+    with pytest.raises(ValueError, match="not outstanding"):
+        dm.wait_ticket(10 ** 6)
+    dm.wait_ticket(dm.record())                      # the ring is free again
+
+
 def test_device_replays_keep_the_inputs():
     """anvil_model_run_device replays the chain on the arena (the bench's device-timed loop): the graph inputs are
     never reused by the memory plan, so after several replays the outputs still equal the oracle's (config c2,
