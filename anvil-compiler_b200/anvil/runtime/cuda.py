@@ -30,7 +30,7 @@ KIND_NAMES = {OP_GEMM: "gemm", OP_LUT: "lut", OP_LUT_MUL: "lut_mul", OP_ADD_REQU
 
 EXPORTS = ("anvil_abi_version", "anvil_last_error", "anvil_device_count", "anvil_cuda_init", "anvil_model_create",
            "anvil_model_prepare", "anvil_model_run", "anvil_model_enqueue", "anvil_model_clear_flags",
-           "anvil_model_wait", "anvil_model_record", "anvil_model_wait_ticket", "anvil_model_selftest_timeout", "anvil_model_run_device", "anvil_model_read",
+           "anvil_model_wait", "anvil_model_record", "anvil_model_wait_ticket", "anvil_model_selftest_timeout", "anvil_model_run_device", "anvil_model_time_launches", "anvil_model_read",
            "anvil_model_write", "anvil_model_read_const", "anvil_model_arena", "anvil_model_describe",
            "anvil_model_free",
            "anvil_gemm_requant")
@@ -74,6 +74,7 @@ def load_library(path: str | os.PathLike | None = None):
             "anvil_model_run": ([vp, ctypes.POINTER(AnvilIO), i32, ctypes.POINTER(AnvilIO), i32,
                                  ctypes.POINTER(ctypes.c_float)], i32),
             "anvil_model_run_device": ([vp, i32, i32, ctypes.POINTER(ctypes.c_float)], i32),
+            "anvil_model_time_launches": ([vp, i32, ctypes.POINTER(ctypes.c_float)], i32),
             "anvil_model_enqueue": ([vp, ctypes.POINTER(AnvilIO), i32, ctypes.POINTER(AnvilIO), i32, vp], i32),
             "anvil_model_clear_flags": ([vp], i32),
             "anvil_model_wait": ([vp], i32),
@@ -173,6 +174,13 @@ class DeviceModel:
     def selftest_timeout(self, wait_ns: int):
         """Run the device wait-bound self-test: raises TimeoutError after about wait_ns (the expected outcome)."""
         check(self.lib.anvil_model_selftest_timeout(self._h, int(wait_ns)), "anvil_model_selftest_timeout")
+
+    def time_launches(self, iters: int = 5) -> list:
+        """Per-launch device microseconds inside CUDA-graph replays of the prepared chain, the shortest of `iters`
+        replays per launch (anvil_model_time_launches)."""
+        us = (ctypes.c_float * max(1, self.n_ops))()
+        check(self.lib.anvil_model_time_launches(self._h, int(iters), us), "anvil_model_time_launches")
+        return [float(us[i]) for i in range(self.n_ops)]
 
     def run_device(self, iters: int = 1, use_graph: bool = True) -> float:
         ms = ctypes.c_float(0)

@@ -1190,6 +1190,69 @@ extern "C" int anvil_model_wait_ticket(anvil_model *m, uint64_t ticket) {
   return check_flags(m, hflags);
 }
 
+// Per-launch device time inside a CUDA-graph replay of the chain: a second graph is captured with a timing event
+// recorded (as an external event node) before the first launch and after every launch, replayed `iters` times on
+// the model's stream, and the shortest time between consecutive events over the replays kept per launch. The launches follow each
+// other as in the chain's own graph, so a launch's figure excludes the host-side launch cost that events around
+// separately issued launches include. The production graph is untouched; the timing graph is freed before return.
+extern "C" int anvil_model_time_launches(anvil_model *m, int iters, float *op_us) {
+  if (!m || iters < 1 || !op_us) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_time_launches");
+  CK(cudaSetDevice(m->device));
+  cudaStream_t st = m->stream;
+  if (int rc = join_copies(m)) return rc;
+  const int n = (int)m->launches.size();
+  if (n == 0) return ANVIL_OK;
+  std::vector<cudaEvent_t> ev(n + 1, nullptr);
+  for (auto &e : ev) CK(cudaEventCreate(&e));
+  auto release = [&](cudaGraphExec_t gx) {
+    if (gx) cudaGraphExecDestroy(gx);
+    for (auto e : ev) cudaEventDestroy(e);
+  };
+  cudaGraph_t g;
+  CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  int rc = ANVIL_OK;
+  cudaError_t e = cudaEventRecordWithFlags(ev[0], st, cudaEventRecordExternal);
+  for (int i = 0; i < n && !rc && e == cudaSuccess; ++i) {
+    rc = launch_op(m, m->launches[i]);
+    if (!rc) e = cudaEventRecordWithFlags(ev[i + 1], st, cudaEventRecordExternal);
+  }
+  cudaError_t e2 = cudaStreamEndCapture(st, &g);
+  if (rc || e != cudaSuccess || e2 != cudaSuccess) {
+    if (e2 == cudaSuccess) cudaGraphDestroy(g);
+    release(nullptr);
+    if (rc) return rc;
+    return fail(ANVIL_E_CUDA, "timing graph capture failed: %s",
+                cudaGetErrorString(e != cudaSuccess ? e : e2));
+  }
+  cudaGraphExec_t gx = nullptr;
+  e = cudaGraphInstantiate(&gx, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    release(nullptr);
+    return fail(ANVIL_E_CUDA, "timing graph instantiate failed: %s", cudaGetErrorString(e));
+  }
+  std::vector<float> best(n, 3.0e38f);
+  CK(cudaMemsetAsync(m->flags, 0, FLAG_WORDS * sizeof(uint32_t), st));
+  for (int it = 0; it < iters; ++it) {
+    if ((e = cudaGraphLaunch(gx, st)) == cudaSuccess) e = cudaStreamSynchronize(st);
+    for (int i = 0; i < n && e == cudaSuccess; ++i) {
+      float t = 0;
+      e = cudaEventElapsedTime(&t, ev[i], ev[i + 1]);
+      best[i] = std::min(best[i], 1000.0f * t);
+    }
+    if (e != cudaSuccess) {
+      release(gx);
+      return fail(ANVIL_E_CUDA, "timing replay failed: %s", cudaGetErrorString(e));
+    }
+  }
+  release(gx);
+  for (int i = 0; i < n; ++i) op_us[i] = best[i];
+  uint32_t hflags[FLAG_WORDS];
+  CK(cudaMemcpyAsync(hflags, m->flags, sizeof hflags, cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  return check_flags(m, hflags);
+}
+
 extern "C" int anvil_model_run_device(anvil_model *m, int iters, int use_graph, float *ms) {
   if (!m || iters < 1) return fail(ANVIL_E_BAD_ARG, "bad arguments to anvil_model_run_device");
   CK(cudaSetDevice(m->device));

@@ -346,13 +346,21 @@ def run_ours(args):
     ms = _max_over_ranks(dist, ms, f"cuda:{local}")
     ms_step = ms / args.steps
     value = ws * tokens / (ms_step / 1000.0)
-    # per-launch device times (CUDA events on the model's stream) for the roofline, taken while the GPU is still at
-    # its working clocks: a burst of graph replays first, then the best of five event-timed runs of the chain
+    # per-launch device times for the roofline, taken while the GPU is still at its working clocks (a burst of graph
+    # replays first): CUDA events recorded inside graph replays of the chain, between consecutive launches (the
+    # launches follow each other as in the timed replays); also, for comparison, events around each launch of
+    # separately issued chains (best of five), which add each launch's host-side issue cost
     dm.run_device(max(20, args.warmup), use_graph=True)
-    kus = None
+    timing_how = "CUDA events recorded inside graph replays of the chain between consecutive launches, best of 10"
+    try:
+        kus_graph = dm.time_launches(10)
+    except Exception as e:                                   # a driver without event nodes in captured graphs
+        kus_graph, timing_how = None, f"events around separately issued launches ({type(e).__name__})"
+    kus_sep = None
     for _ in range(5):
         k = dm.run([(off, xin)], [], timing=True)
-        kus = k if kus is None else [min(a, b) for a, b in zip(kus, k)]
+        kus_sep = k if kus_sep is None else [min(a, b) for a, b in zip(kus_sep, k)]
+    kus = kus_graph if kus_graph is not None else kus_sep
     if want is not None:
         _gate(cm, prog, dm, sample, want, "after the timed replays")
     hbm, bf16, src = _peaks()
@@ -432,6 +440,8 @@ def run_ours(args):
             "roofline_norm": norm_roof,
             "kernel_us_by_kind": dict(sorted(by_kind.items(), key=lambda kv: -kv[1])),
             "launch_us": [[d.label, C.KIND_NAMES[d.kind], round(u, 2)] for d, u in zip(prog.devops, kus)],
+            "launch_timing": timing_how,
+            "launch_us_separate": [round(u, 2) for u in kus_sep],
             "gpu_launches": sum(1 for d in prog.devops if d.kind != C.OP_COPY) * args.steps,
             "clocks": clk.summary()}
     if strong is not None:

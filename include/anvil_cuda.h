@@ -150,6 +150,14 @@ ANVIL_API int anvil_model_run(anvil_model *m, const anvil_io *inputs, int n_inpu
  * (CUDA events on the model's stream) in *ms. Used by benchmarks to time kernels with inputs already in HBM. */
 ANVIL_API int anvil_model_run_device(anvil_model *m, int iters, int use_graph, float *ms);
 
+/* Benchmark-only: each launch's device time inside a CUDA-graph replay of the prepared chain on the arena as it is
+ * (a timing graph with an event recorded before the first launch and after each one, replayed `iters` times,
+ * synchronised after each replay); op_us[i] = the shortest time of launch i over the replays, in microseconds
+ * (n_ops floats, as prepared).
+ * Device checks are reported as by anvil_model_run. The per-launch timing of the reference's RunOutput.cycles
+ * (anvil/driver.py:56-76) at graph-replay launch cost; no separate reference entry point. */
+ANVIL_API int anvil_model_time_launches(anvil_model *m, int iters, float *op_us);
+
 /* The run of anvil_model_run split for pipelines over several models (each its own arena and stream): the H2D
  * copies of `inputs`, the launch chain (one CUDA graph launch, captured on first use) and the D2H copies of
  * `outputs`, returning without waiting. The copies go to the device's two shared copy streams (one per direction,

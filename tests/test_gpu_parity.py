@@ -285,6 +285,31 @@ def test_completion_tickets_are_bounded_and_single_use():
     dm.wait_ticket(dm.record())                      # the ring is free again
 
 
+def test_launch_times_inside_a_graph_replay():
+    """anvil_model_time_launches: one figure per prepared launch, non-negative, and together about as long as a replay
+    of the chain's own graph (the timing graph adds only its event nodes); the arena still gives the oracle's
+    outputs afterwards."""
+    from anvil.driver import _apply_view
+    module, consts, body = _frozen()
+    rng = np.random.default_rng(25)
+    xs = rng.integers(-(1 << 15), 1 << 15, (8,) + np.shape(body["x"]))
+    want = interp.run(module, {"x": xs}, consts, batch=True)
+    cm = anvil.compile(module, consts=consts)
+    prog = cm.program(8)
+    dm = cm._device_model(0)
+    dm.prepare(prog.ops, prog.plan.arena, key=(8, "outputs", False))
+    dm.write(prog.inputs["x"][0], np.ascontiguousarray(xs, dtype=np.int16))
+    us = dm.time_launches(5)
+    assert len(us) == len(prog.ops) and min(us) >= 0 and sum(us) > 0
+    replay_us = 1000 * dm.run_device(20, use_graph=True) / 20
+    assert sum(us) <= 3 * replay_us + 50, (sum(us), replay_us)
+    for sym, v in prog.outputs:
+        if sym is None or v.const:
+            continue
+        buf = dm.read(prog.plan.addresses[v.root], np.empty(prog.buffers[v.root], dtype=np.uint8))
+        assert np.array_equal(_apply_view(buf, v), want.values[sym]), sym
+
+
 def test_device_replays_keep_the_inputs():
     """anvil_model_run_device replays the chain on the arena (the bench's device-timed loop): the graph inputs are
     never reused by the memory plan, so after several replays the outputs still equal the oracle's (config c2,
